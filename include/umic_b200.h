@@ -1,0 +1,181 @@
+/*
+ * umic_b200.h -- C ABI of the B200 (sm_100a) fused-inference hot path.
+ *
+ * Every entry point:
+ *   - takes raw device pointers, element strides (in elements, not bytes) and a
+ *     cudaStream_t (passed as void*; NULL = legacy default stream);
+ *   - launches asynchronously on that stream, performs no host synchronisation
+ *     and no device allocation, so it is safe inside CUDA-graph capture;
+ *   - returns 0 on success or one of the UMIC_ERR_* codes below. The code is
+ *     decided on the host before launch (shape / stride / alignment checks) or
+ *     comes from the launch itself. umic_last_error_message() gives a one-line
+ *     reason for the last non-zero return on the calling thread.
+ *
+ * Tensors are bf16 unless a dtype argument says otherwise. "Rows" are the
+ * flattened leading dimensions; the last dimension must be contiguous.
+ *
+ * Each function names the reference interface it replaces
+ * (soonhong99/umic-alpamayo, paths relative to that project's root).
+ */
+#ifndef UMIC_B200_H_
+#define UMIC_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define UMIC_API __attribute__((visibility("default")))
+#else
+#define UMIC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UMIC_OK 0
+#define UMIC_ERR_INVALID_ARG 1  /* null pointer, negative or zero size */
+#define UMIC_ERR_UNSUPPORTED 2  /* shape the kernel does not handle */
+#define UMIC_ERR_ALIGNMENT 3    /* pointer or stride breaks a 16-byte rule */
+#define UMIC_ERR_LAUNCH 4       /* CUDA reported an error at launch */
+#define UMIC_ERR_OVERFLOW 5     /* KV append past the buffer capacity */
+#define UMIC_ERR_DEVICE 6       /* no sm_100 device / driver entry point */
+
+/* Device-side error bits, read with umic_device_errors(). */
+#define UMIC_DEVERR_KV_OVERFLOW 1u   /* device-position KV append out of range */
+#define UMIC_DEVERR_WAIT_TIMEOUT 2u  /* a bounded mbarrier wait ran out */
+
+/* dtype codes for optional fp32 side inputs */
+#define UMIC_DTYPE_BF16 0
+#define UMIC_DTYPE_FP32 1
+
+/* GEMM epilogues */
+#define UMIC_EPI_NONE 0
+#define UMIC_EPI_GELU_ERF 1   /* 0.5*x*(1+erf(x/sqrt2)), linear.py:83-86 */
+#define UMIC_EPI_GELU_TANH 2  /* tanh approximation (HF gelu_pytorch_tanh) */
+
+/* ---- library ------------------------------------------------------------ */
+
+/* ABI version: bumps when a signature changes. */
+UMIC_API int umic_abi_version(void);
+
+/* One-line reason for the last non-zero return on this thread ("" if none). */
+UMIC_API const char* umic_last_error_message(void);
+
+/* Makes `device` the current device of this library's CUDA runtime for the
+ * calling thread (the library links its own runtime; the host wrapper calls
+ * this when a tensor lives on another GPU than the previous call's).
+ * No reference counterpart: the reference runs on one device. */
+UMIC_API int umic_set_device(int device);
+
+/* Reads the device-side error word of the current device into *flags
+ * (synchronises the device). If clear != 0 the word is reset to 0.
+ * No reference counterpart: the reference raises Python exceptions only. */
+UMIC_API int umic_device_errors(uint32_t* flags, int clear);
+
+/* ---- RMSNorm family (src/umic/kernels/rmsnorm.py) ------------------------ */
+
+/* y = bf16(x * rsqrt(mean(x^2) + eps) * w), fp32 inside.
+ * Replaces rmsnorm_triton / _rmsnorm_kernel (rmsnorm.py:32-73).
+ * w_dtype: UMIC_DTYPE_BF16 or UMIC_DTYPE_FP32. */
+UMIC_API int umic_rmsnorm(const void* x, int64_t x_row_stride, const void* w, int w_dtype,
+                 void* y, int64_t y_row_stride, int64_t rows, int64_t n, float eps,
+                 void* stream);
+
+/* s = x + r (fp32); summed = bf16(s); normed = bf16(s * rsqrt(mean(s^2)+eps) * w).
+ * Replaces add_rmsnorm_triton / _add_rmsnorm_kernel (rmsnorm.py:75-134). */
+UMIC_API int umic_add_rmsnorm(const void* x, int64_t x_row_stride, const void* r,
+                     int64_t r_row_stride, const void* w, int w_dtype, void* normed,
+                     int64_t normed_row_stride, void* summed, int64_t summed_row_stride,
+                     int64_t rows, int64_t n, float eps, void* stream);
+
+/* ---- LayerNorm family (src/umic/kernels/layernorm.py) -------------------- */
+
+/* y = bf16((x - mean) * rsqrt(var + eps) * w + b), fp32 inside; w and b share
+ * w_dtype. Replaces layernorm_triton / _layernorm_kernel (layernorm.py:31-68). */
+UMIC_API int umic_layernorm(const void* x, int64_t x_row_stride, const void* w, const void* b,
+                   int w_dtype, void* y, int64_t y_row_stride, int64_t rows, int64_t n,
+                   float eps, void* stream);
+
+/* add + LayerNorm with two outputs (normed, summed).
+ * Replaces add_layernorm_triton / _add_layernorm_kernel (layernorm.py:70-124). */
+UMIC_API int umic_add_layernorm(const void* x, int64_t x_row_stride, const void* r,
+                       int64_t r_row_stride, const void* w, const void* b, int w_dtype,
+                       void* normed, int64_t normed_row_stride, void* summed,
+                       int64_t summed_row_stride, int64_t rows, int64_t n, float eps,
+                       void* stream);
+
+/* ---- rotary embedding, in place (src/umic/kernels/rope.py) --------------- */
+
+/* In-place rotate-half RoPE on q and (optionally) k:
+ *   out[d]       = x[d]*cos[d]         - x[d+D/2]*sin[d]
+ *   out[d+D/2]   = x[d+D/2]*cos[d+D/2] + x[d]*sin[d+D/2]      (d < D/2)
+ * fp32 inside, one bf16 rounding. q is indexed [batch, seq, head, dim] through
+ * (q_sb, q_ss, q_sh) element strides with dim contiguous; k likewise (k may be
+ * NULL with hk = 0). cos/sin are [batch, seq, dim] through (c_sb, c_ss), in
+ * cos_dtype (bf16 for HF text RoPE, fp32 for HF vision RoPE); c_sb may be 0 to
+ * broadcast one table over the batch.
+ * Replaces _rope_kernel/_apply_one (rope.py:31-76), apply_rotary_vision_triton
+ * (rope.py:78-84) and the text path of make_text_rope (rope.py:86-107), which
+ * were out-of-place. */
+UMIC_API int umic_rope_inplace(void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, int32_t hq,
+                      void* k, int64_t k_sb, int64_t k_ss, int64_t k_sh, int32_t hk,
+                      const void* cos, const void* sin, int64_t c_sb, int64_t c_ss,
+                      int cos_dtype, int64_t batch, int64_t seq, int32_t head_dim,
+                      void* stream);
+
+/* ---- KV cache (src/umic/cache.py) ----------------------------------------- */
+
+/* Writes n_new tokens of k_new / v_new into the preallocated buffers at token
+ * position pos (host value) or *dpos (device int64, read at execution time so a
+ * captured graph can replay at a moving position; pass dpos = NULL to use pos).
+ * Buffers are [batch, heads, capacity, head_dim] through (buf_sb, buf_sh,
+ * buf_ss) element strides; k_new / v_new are [batch, heads, n_new, head_dim]
+ * through their own strides. A host position past capacity returns
+ * UMIC_ERR_OVERFLOW without launching; a device position past capacity skips
+ * the write and sets UMIC_DEVERR_KV_OVERFLOW.
+ * Replaces InplaceLayer.update's writes (cache.py:50-80: slice assignment and the
+ * graph-mode index_copy_ at cache.py:59-60). */
+UMIC_API int umic_kv_append(void* k_buf, void* v_buf, int64_t buf_sb, int64_t buf_sh,
+                   int64_t buf_ss, int64_t capacity, const void* k_new, int64_t kn_sb,
+                   int64_t kn_sh, int64_t kn_ss, const void* v_new, int64_t vn_sb,
+                   int64_t vn_sh, int64_t vn_ss, int64_t batch, int32_t heads,
+                   int64_t n_new, int32_t head_dim, int64_t pos, const int64_t* dpos,
+                   void* stream);
+
+/* ---- projections (src/umic/kernels/linear.py, fused_ffn.py) -------------- */
+
+/* Row-count regime below FUSE_MIN_ROWS (integrate.py:27-30): HBM-bound GEMV,
+ * y[m, n] = sum_k x[m, k] * w[n, k] (+ bias[n]); m < 64. w is [n, k] row-major
+ * (nn.Linear layout). Replaces the cuBLAS fallback of _patched_linear_forward
+ * (integrate.py:104-105). bias may be NULL. */
+UMIC_API int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+              void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* stream);
+
+/* h[m, n] = silu(x . wg[n]) * (x . wu[n]) for m < 64 rows.
+ * Replaces the small-row branch of _fused_mlp_forward (integrate.py:48-50). */
+UMIC_API int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg, const void* wu,
+                            int64_t ldw, void* h, int64_t ldh, int64_t m, int64_t n,
+                            int64_t k, void* stream);
+
+/* Tensor-core (tcgen05 + TMEM, TMA-fed) GEMM: y = epi(x . w^T + bias) + residual.
+ * x [m, k], w [n, k] (both K-major), y [m, n]. bias / residual may be NULL.
+ * epilogue: UMIC_EPI_*. Requires k % 8 == 0, n % 8 == 0, leading dimensions that
+ * are multiples of 8 elements and 16-byte aligned base pointers.
+ * Replaces linear_triton / _linear_kernel (linear.py:32-145). */
+UMIC_API int umic_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+              const void* residual, int64_t ldr, void* y, int64_t ldy, int64_t m,
+              int64_t n, int64_t k, int epilogue, void* stream);
+
+/* Dual-accumulator tensor-core GEMM with the SwiGLU epilogue in registers:
+ * h = silu(x . wg^T) * (x . wu^T); the gate and up products never reach HBM.
+ * wg / wu are [n, k] (nn.Linear layout). Same alignment rules as umic_gemm.
+ * Replaces gate_silu_mul_triton / _gate_silu_mul_kernel (fused_ffn.py:48-118). */
+UMIC_API int umic_gemm_gate_silu_mul(const void* x, int64_t ldx, const void* wg, int64_t ldwg,
+                            const void* wu, int64_t ldwu, void* h, int64_t ldh,
+                            int64_t m, int64_t n, int64_t k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UMIC_B200_H_ */

@@ -1,0 +1,70 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol the header
+declares, and rejects bad arguments on the host before touching a GPU."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from umic_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "umic_b200.h"
+
+
+def _declared() -> list[str]:
+    return re.findall(r"UMIC_API\s+(?:int|const char\*)\s+(umic_\w+)\(", HEADER.read_text())
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    declared = _declared()
+    assert len(declared) >= 14
+    for name in declared:
+        assert hasattr(L, name), f"{name} declared in the header but not exported"
+    assert set(declared) == set(_lib.exported_symbols())
+
+
+def test_abi_version():
+    assert _lib.lib().umic_abi_version() == 1
+
+
+def test_null_pointer_rejected_on_host():
+    L = _lib.lib()
+    rc = L.umic_rmsnorm(None, 8, None, 0, None, 8, 4, 8, ctypes.c_float(1e-6), None)
+    assert rc == 1
+    assert "null" in _lib.last_message()
+
+
+def test_bad_sizes_rejected_on_host():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(16)  # never dereferenced: the size check fails first
+    assert L.umic_gemm(fake, 8, fake, 8, None, None, 0, fake, 8, 4, 4, 0, 0, None) == 1
+    assert L.umic_gemm(fake, 12, fake, 12, None, None, 0, fake, 16, 4, 16, 12, 0, None) == 3
+    assert "multiple of 8" in _lib.last_message()
+    assert L.umic_gemv(fake, 8, fake, 8, None, fake, 8, 65, 8, 8, None) == 2
+    assert L.umic_rope_inplace(fake, 0, 0, 0, 1, None, 0, 0, 0, 0, fake, fake, 0, 0, 0, 1, 1, 7,
+                               None) == 1
+    assert L.umic_kv_append(fake, fake, 0, 0, 0, 10, fake, 0, 0, 0, fake, 0, 0, 0, 1, 1, 4, 8,
+                            8, None, None) == 5
+    assert "overflow" in _lib.last_message()
+
+
+def test_empty_work_is_a_noop():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(16)
+    assert L.umic_rmsnorm(fake, 8, fake, 0, fake, 8, 0, 8, ctypes.c_float(1e-6), None) == 0
+    assert L.umic_gemm(fake, 8, fake, 8, None, None, 0, fake, 8, 0, 8, 8, 0, None) == 0
+
+
+def test_kernel_wrappers_refuse_cpu_tensors():
+    import torch
+
+    from umic_b200.kernels import linear, rmsnorm
+
+    x = torch.zeros(4, 8, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        rmsnorm(x, torch.ones(8, dtype=torch.bfloat16), 1e-6)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        linear(x, torch.zeros(8, 8, dtype=torch.bfloat16))

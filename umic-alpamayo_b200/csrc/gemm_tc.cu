@@ -1,0 +1,567 @@
+// Tensor-core GEMM for sm_100a: tcgen05.mma with TMEM accumulators, fed by TMA.
+//
+//   y[m, n] = epi(sum_k x[m, k] * w[n, k] + bias[n]) + residual[m, n]    (linear)
+//   h[m, n] = silu(x . wg[n]) * (x . wu[n])                              (gate/up)
+//
+// Both operands are K-major (activations [m, k] row-major, nn.Linear weights
+// [n, k] row-major), so no transpose or copy of the weights is ever made.
+//
+// Persistent kernel, one CTA per SM, 6 warps with fixed roles:
+//   warp 0     TMA producer: fills a 4-stage shared-memory ring of
+//              (A 128x64, B 256x64) bf16 tiles, 128-byte swizzled;
+//   warp 1     allocates 512 TMEM columns; one lane issues tcgen05.mma
+//              (M=128, N=256, K=16; 4 per 64-wide k-block) and commits each
+//              stage back to the producer through an mbarrier;
+//   warps 2-5  epilogue: tcgen05.ld of the fp32 accumulator (each warp reads
+//              its 32-lane TMEM quarter), bias / activation / residual in
+//              registers, bf16 stores.
+// The accumulator is double-buffered in TMEM (2 x 256 columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Gate/up: the B stage holds 128 rows of w_gate followed by 128 rows of w_up
+// (two TMA loads into adjacent 16 KB halves). One N=256 MMA then produces the
+// gate accumulator in TMEM columns 0-127 and the up accumulator in 128-255;
+// the epilogue combines them as silu(g) * u, so neither product reaches HBM
+// (the reference's dual accumulators, fused_ffn.py:68-87).
+//
+// Tiles are walked in groups of kGroupM row-blocks (row-block fastest) so a
+// wave of CTAs shares both its activation rows and its weight columns in L2
+// (the reference's GROUP swizzle, linear.py:43-55).
+//
+// Every mbarrier wait is bounded (about 5 s of SM clock); a wait that runs
+// out sets UMIC_DEVERR_WAIT_TIMEOUT, the CTA drains its outstanding work,
+// frees its TMEM and exits instead of hanging.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace umic {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;  // MMA N (output tile width for linear; 2 x 128 for gate/up)
+constexpr int kBK = 64;   // one 128-byte swizzle atom of bf16
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kABytes = kBM * kBK * 2;       // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;       // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr size_t kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr long long kWaitLimitCycles = 10000000000LL;
+
+struct TcParams {
+  __nv_bfloat16* y;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;
+  int64_t ldy, ldr;
+  uint32_t* err;
+  int m, n, k;
+  int tiles_m, tiles_n;  // output tiles
+  int kblocks;
+  int epilogue;
+};
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete. Returns false
+// (after flagging the error word and the CTA abort flag) if it never does.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err,
+                                          volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const long long start = clock64();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (clock64() - start > kWaitLimitCycles) {
+        *abort_flag = 1;
+        if (err) atomicOr(err, UMIC_DEVERR_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row
+// core-matrix groups 1024 bytes apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;           // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;   // SBO
+  d |= static_cast<uint64_t>(1) << 46;           // version
+  d |= static_cast<uint64_t>(2) << 61;           // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D fp32, A/B bf16, both K-major, N=256, M=128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kBN >> 3) << 17) |
+                            ((kBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns; thread i receives lane (base + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, int& nb) {
+  const int per_group = kGroupM * p.tiles_n;
+  const int g = t / per_group;
+  const int first = g * kGroupM;
+  const int gm = min(p.tiles_m - first, kGroupM);
+  const int r = t - g * per_group;
+  mb = first + r % gm;
+  nb = r / gm;
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+}
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.f + tanhf(u));
+}
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+
+// ------------------------------------------------------------------ kernel
+
+template <bool kDual>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                   const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_b2, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  // bars: full[kStages], empty[kStages], acc_full[2], acc_empty[2], drain
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages);
+  const uint32_t accf0 = smem_u32(bars + 2 * kStages), acce0 = accf0 + 16;
+  const uint32_t drain = accf0 + 32;
+  const uint32_t sbase = smem_u32(smem);
+  const int tiles = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(accf0, 1);
+    mbar_init(accf0 + 8, 1);
+    mbar_init(acce0, 128);
+    mbar_init(acce0 + 8, 128);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    prefetch_map(&map_a);
+    prefetch_map(&map_b);
+    if (kDual) prefetch_map(&map_b2);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_stage = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, p, mb, nb);
+        const int row_a = mb * kBM;
+        const int row_b = kDual ? nb * (kBN / 2) : nb * kBN;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8 * stage;
+          const uint32_t sa = sbase + stage * kStageBytes;
+          const uint32_t sb = sa + kABytes;
+          mbar_expect_tx(fb, kStageBytes);
+          tma_load_2d(sa, &map_a, fb, kb * kBK, row_a);
+          if (kDual) {
+            tma_load_2d(sb, &map_b, fb, kb * kBK, row_b);
+            tma_load_2d(sb + kBBytes / 2, &map_b2, fb, kb * kBK, row_b);
+          } else {
+            tma_load_2d(sb, &map_b, fb, kb * kBK, row_b);
+          }
+          issued_stage = stage;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok && issued_stage >= 0) {
+        // Aborting: give the copies already in flight time to land (they take
+        // microseconds) before this CTA's shared memory is released.
+        const long long t0 = clock64();
+        while (clock64() - t0 < 4000000LL) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * kBN;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(full0 + 8 * stage, phase, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sbase + stage * kStageBytes;
+          const uint64_t ad = sdesc(sa), bd = sdesc(sa + kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // +32 bytes along K inside the swizzle atom = +2 in the >>4 field
+            mma_bf16(tmem_d, ad + 2 * kk, bd + 2 * kk, (kb | kk) ? 1u : 0u);
+          }
+          mma_commit(empty0 + 8 * stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mma_commit(accf0 + 8 * acc);
+      }
+      // Wait for every MMA issued by this thread before TMEM is released.
+      mma_commit(drain);
+      mbar_wait(drain, 0, p.err, abort_flag);
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      int mb, nb;
+      tile_coords(t, p, mb, nb);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(accf0 + 8 * acc, acc_phase, p.err, abort_flag)) break;
+      tc_fence_after();
+      const int row = mb * kBM + quarter * 32 + lane;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
+      constexpr int kOutCols = kDual ? kBN / 2 : kBN;
+      const int col0 = nb * kOutCols;
+#pragma unroll 1
+      for (int c = 0; c < kOutCols; c += 32) {
+        __syncwarp();  // tcgen05.ld is warp-collective
+        float v[32];
+        tmem_ld32(tbase + c, v);
+        if (kDual) {
+          float u[32];
+          tmem_ld32(tbase + kBN / 2 + c, u);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = silu(v[i]) * u[i];
+        }
+        if (c + 32 >= kOutCols) {
+          // All TMEM reads of this tile are done: hand the buffer back.
+          tc_fence_before();
+          mbar_arrive(acce0 + 8 * acc);
+        }
+        if (row >= p.m) continue;  // rows past m: no stores (TMA read zeros there)
+        const int cbase = col0 + c;
+        if (!kDual) {
+          if (p.bias) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              if (cbase + i < p.n) {
+                float b[8];
+                unpack8(ld_cached(p.bias + cbase + i), b);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i + j] += b[j];
+              }
+            }
+          }
+          if (p.epilogue == UMIC_EPI_GELU_ERF) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+          } else if (p.epilogue == UMIC_EPI_GELU_TANH) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+          }
+          if (p.residual) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              if (cbase + i < p.n) {
+                float r[8];
+                unpack8(ld_stream(p.residual + static_cast<int64_t>(row) * p.ldr + cbase + i), r);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i + j] += r[j];
+              }
+            }
+          }
+        }
+        __nv_bfloat16* out = p.y + static_cast<int64_t>(row) * p.ldy + cbase;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          if (cbase + i < p.n) {
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = v[i + j];
+            st_vec(out + i, pack8(o));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols));
+  }
+}
+
+// --------------------------------------------------------------------- host
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// 2-D bf16 K-major operand [rows, k] with row stride ld (elements); box of
+// box_rows x 64, 128-byte swizzle, out-of-range elements read as zero.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int64_t ld,
+              int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool kDual>
+int set_smem_attr() {
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  cudaError_t e = cudaSuccess;
+  std::call_once(once[dev], [&] {
+    e = cudaFuncSetAttribute(tc_gemm_kernel<kDual>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes));
+  });
+  if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "tc_gemm smem attribute: %s",
+                                    cudaGetErrorString(e));
+  return UMIC_OK;
+}
+
+int check_operand(const char* name, const char* what, const void* p, int64_t ld, int64_t k) {
+  if (!p) return fail(UMIC_ERR_INVALID_ARG, "%s: %s is NULL", name, what);
+  if (!aligned16(p)) return fail(UMIC_ERR_ALIGNMENT, "%s: %s not 16-byte aligned", name, what);
+  if (ld % 8) return fail(UMIC_ERR_ALIGNMENT, "%s: ld of %s not a multiple of 8", name, what);
+  if (ld < k) return fail(UMIC_ERR_INVALID_ARG, "%s: ld of %s < k", name, what);
+  return UMIC_OK;
+}
+
+template <bool kDual>
+int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw,
+        const void* w2, int64_t ldw2, const void* bias, const void* residual, int64_t ldr,
+        void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, int epilogue, void* stream) {
+  clear_error();
+  if (m < 0 || n < 0 || k <= 0) return fail(UMIC_ERR_INVALID_ARG, "%s: bad sizes", name);
+  if (m == 0 || n == 0) return UMIC_OK;
+  if (m > 0x7fffffffLL - kBM || n > 0x7fffffffLL - kBN || k > 0x7fffffffLL)
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: size too large", name);
+  if (k % 8) return fail(UMIC_ERR_ALIGNMENT, "%s: k=%lld not a multiple of 8", name,
+                         (long long)k);
+  if (n % 8) return fail(UMIC_ERR_UNSUPPORTED, "%s: n=%lld not a multiple of 8", name,
+                         (long long)n);
+  if (int rc = check_operand(name, "x", x, ldx, k)) return rc;
+  if (int rc = check_operand(name, "w", w, ldw, k)) return rc;
+  if (kDual)
+    if (int rc = check_operand(name, "w_up", w2, ldw2, k)) return rc;
+  if (!y || !aligned16(y) || ldy % 8 || ldy < n)
+    return fail(UMIC_ERR_ALIGNMENT, "%s: output must be 16-byte aligned with ld %% 8 == 0", name);
+  if (bias && !aligned16(bias)) return fail(UMIC_ERR_ALIGNMENT, "%s: bias alignment", name);
+  if (residual && (!aligned16(residual) || ldr % 8 || ldr < n))
+    return fail(UMIC_ERR_ALIGNMENT, "%s: residual alignment", name);
+  if (epilogue < UMIC_EPI_NONE || epilogue > UMIC_EPI_GELU_TANH)
+    return fail(UMIC_ERR_INVALID_ARG, "%s: bad epilogue %d", name, epilogue);
+
+  const int out_cols = kDual ? kBN / 2 : kBN;
+  CUtensorMap ma, mb, mb2;
+  if (!make_map(&ma, x, m, k, ldx, kBM) ||
+      !make_map(&mb, w, n, k, ldw, kDual ? kBN / 2 : kBN) ||
+      !make_map(&mb2, kDual ? w2 : w, n, k, kDual ? ldw2 : ldw, kDual ? kBN / 2 : kBN))
+    return fail(UMIC_ERR_DEVICE, "%s: cuTensorMapEncodeTiled unavailable or rejected", name);
+  if (int rc = set_smem_attr<kDual>()) return rc;
+
+  TcParams p;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.ldy = ldy;
+  p.ldr = ldr;
+  p.err = device_error_word();
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.tiles_m = static_cast<int>((m + kBM - 1) / kBM);
+  p.tiles_n = static_cast<int>((n + out_cols - 1) / out_cols);
+  p.kblocks = static_cast<int>((k + kBK - 1) / kBK);
+  p.epilogue = epilogue;
+  const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  if (tiles > 0x7fffffffLL) return fail(UMIC_ERR_UNSUPPORTED, "%s: too many tiles", name);
+  const int sms = sm_count();
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  tc_gemm_kernel<kDual><<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(ma, mb, mb2, p);
+  return launch_status(name);
+}
+
+}  // namespace
+}  // namespace umic
+
+using namespace umic;
+
+extern "C" {
+
+int umic_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+              const void* residual, int64_t ldr, void* y, int64_t ldy, int64_t m, int64_t n,
+              int64_t k, int epilogue, void* stream) {
+  return run<false>("umic_gemm", x, ldx, w, ldw, nullptr, 0, bias, residual, ldr, y, ldy, m, n, k,
+                    epilogue, stream);
+}
+
+int umic_gemm_gate_silu_mul(const void* x, int64_t ldx, const void* wg, int64_t ldwg,
+                            const void* wu, int64_t ldwu, void* h, int64_t ldh, int64_t m,
+                            int64_t n, int64_t k, void* stream) {
+  return run<true>("umic_gemm_gate_silu_mul", x, ldx, wg, ldwg, wu, ldwu, nullptr, nullptr, 0, h,
+                   ldh, m, n, k, UMIC_EPI_NONE, stream);
+}
+
+}  // extern "C"

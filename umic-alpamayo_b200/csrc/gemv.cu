@@ -1,0 +1,220 @@
+// Decode-regime projection (rows < FUSE_MIN_ROWS): y[m, n] = x[m, :] . w[n, :].
+//
+// HBM-bound: every weight byte is read once, the activations (m <= 63 rows)
+// stay in L1/L2. The dot products run on the tensor cores through
+// mma.sync.m16n8k16 so the math costs nothing next to the weight stream:
+//   - a warp owns 16 weight rows; the 8 activation rows of an m-chunk are the
+//     n8 side of the MMA; m <= 63 uses up to 8 chunks that reuse the weight
+//     registers;
+//   - lane (g = lane/4, t = lane%4) loads w[n0+g][k+8t .. k+8t+7] and
+//     w[n0+g+8][...] as two 16-byte vectors, and x[g][k+8t .. +7] as one.
+//     A dot product does not depend on the order of its k terms, so the same
+//     permutation of k applied to both operands lets these 16-byte loads be
+//     the MMA fragments directly (two m16n8k16 steps per 32-wide k slab), with
+//     no shared-memory staging and no bf16->fp32 conversions;
+//   - the warps of a CTA split k into contiguous ranges and meet in shared
+//     memory at the end.
+// The gated variant streams gate and up rows together and applies
+// silu(g) * u before the single bf16 rounding (fused_ffn.py:86-87 semantics).
+#include "common.cuh"
+
+namespace umic {
+namespace {
+
+struct GemvArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w;   // gate when gated
+  const __nv_bfloat16* w2;  // up when gated
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* y;
+  int64_t ldx, ldw, ldy;
+  int m, n, k;
+  int slabs;  // ceil(k / 32)
+};
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two k16 steps from one 32-wide slab: rows g / g+8 of w (wlo / whi) and
+// row g of x, each 8 consecutive k values held as a uint4.
+__device__ __forceinline__ void slab_mma(float (&c)[4], const uint4& wlo, const uint4& whi,
+                                         const uint4& xv) {
+  mma16816(c, wlo.x, whi.x, wlo.y, whi.y, xv.x, xv.y);
+  mma16816(c, wlo.z, whi.z, wlo.w, whi.w, xv.z, xv.w);
+}
+
+constexpr int kUnroll = 4;
+
+template <int MC, bool kGated>
+__global__ void __launch_bounds__(512) gemv_kernel(GemvArgs a) {
+  extern __shared__ float red[];  // [warps][kGated+1][MC][4][32]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int n0 = blockIdx.x * 16;
+  const int r0 = n0 + g, r1 = n0 + g + 8;
+  const bool r0ok = r0 < a.n, r1ok = r1 < a.n;
+
+  float acc[MC][4];
+  float acc2[kGated ? MC : 1][4];
+#pragma unroll
+  for (int i = 0; i < MC; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[i][j] = 0.f;
+      if constexpr (kGated) acc2[i][j] = 0.f;
+    }
+
+  // Contiguous slab range of this warp.
+  const int per = (a.slabs + nwarps - 1) / nwarps;
+  const int s_begin = warp * per;
+  const int s_end = min(a.slabs, s_begin + per);
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+
+  for (int s0 = s_begin; s0 < s_end; s0 += kUnroll) {
+    uint4 wl[kUnroll], wh[kUnroll], ul[kGated ? kUnroll : 1], uh[kGated ? kUnroll : 1];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int kk = (s0 + u) * 32 + t * 8;
+      const bool kok = (s0 + u) < s_end && kk < a.k;
+      wl[u] = (kok && r0ok) ? ld_stream(a.w + r0 * a.ldw + kk) : zero;
+      wh[u] = (kok && r1ok) ? ld_stream(a.w + r1 * a.ldw + kk) : zero;
+      if constexpr (kGated) {
+        ul[u] = (kok && r0ok) ? ld_stream(a.w2 + r0 * a.ldw + kk) : zero;
+        uh[u] = (kok && r1ok) ? ld_stream(a.w2 + r1 * a.ldw + kk) : zero;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int kk = (s0 + u) * 32 + t * 8;
+      const bool kok = (s0 + u) < s_end && kk < a.k;
+#pragma unroll
+      for (int mc = 0; mc < MC; ++mc) {
+        const int xr = mc * 8 + g;
+        const uint4 xv = (kok && xr < a.m) ? ld_cached(a.x + xr * a.ldx + kk) : zero;
+        slab_mma(acc[mc], wl[u], wh[u], xv);
+        if constexpr (kGated) slab_mma(acc2[mc], ul[u], uh[u], xv);
+      }
+    }
+  }
+
+  // Cross-warp reduction of the C fragments.
+  constexpr int kAcc = kGated ? 2 : 1;
+  float* mine = red + static_cast<size_t>(warp) * kAcc * MC * 4 * 32;
+#pragma unroll
+  for (int mc = 0; mc < MC; ++mc)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      mine[(mc * 4 + j) * 32 + lane] = acc[mc][j];
+      if constexpr (kGated) mine[((MC + mc) * 4 + j) * 32 + lane] = acc2[mc][j];
+    }
+  __syncthreads();
+  if (warp != 0) return;
+  const int stride = kAcc * MC * 4 * 32;
+#pragma unroll
+  for (int mc = 0; mc < MC; ++mc) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v = 0.f, v2 = 0.f;
+      for (int w = 0; w < nwarps; ++w) {
+        v += red[w * stride + (mc * 4 + j) * 32 + lane];
+        if constexpr (kGated) v2 += red[w * stride + ((MC + mc) * 4 + j) * 32 + lane];
+      }
+      // C fragment: c0,c1 -> (row g, cols 2t,2t+1); c2,c3 -> (row g+8, ...)
+      const int nrow = (j < 2) ? r0 : r1;
+      const int mcol = mc * 8 + 2 * t + (j & 1);
+      if (nrow >= a.n || mcol >= a.m) continue;
+      float o;
+      if constexpr (kGated) {
+        o = v / (1.f + __expf(-v)) * v2;
+      } else {
+        o = v;
+        if (a.bias) o += bf(a.bias[nrow]);
+      }
+      a.y[mcol * a.ldy + nrow] = __float2bfloat16_rn(o);
+    }
+  }
+}
+
+template <int MC, bool kGated>
+int launch(const GemvArgs& a, cudaStream_t st) {
+  const int ctas = (a.n + 15) / 16;
+  // Enough warps per SM to keep ~64 KB of weight loads in flight.
+  int warps = (ctas >= 2 * sm_count()) ? 8 : 16;
+  const size_t smem = static_cast<size_t>(warps) * (kGated ? 2 : 1) * MC * 4 * 32 * sizeof(float);
+  static_assert(sizeof(float) == 4, "");
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(gemv_kernel<MC, kGated>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+  gemv_kernel<MC, kGated><<<ctas, warps * 32, smem, st>>>(a);
+  return launch_status("umic_gemv launch");
+}
+
+template <bool kGated>
+int dispatch(const GemvArgs& a, cudaStream_t st) {
+  switch ((a.m + 7) / 8) {
+    case 1: return launch<1, kGated>(a, st);
+    case 2: return launch<2, kGated>(a, st);
+    case 3: return launch<3, kGated>(a, st);
+    case 4: return launch<4, kGated>(a, st);
+    case 5: return launch<5, kGated>(a, st);
+    case 6: return launch<6, kGated>(a, st);
+    case 7: return launch<7, kGated>(a, st);
+    case 8: return launch<8, kGated>(a, st);
+  }
+  return fail(UMIC_ERR_UNSUPPORTED, "umic_gemv: m=%d outside 1..64", a.m);
+}
+
+int check(const char* name, const void* x, int64_t ldx, const void* w, const void* w2,
+          int64_t ldw, const void* y, int64_t ldy, int64_t m, int64_t n, int64_t k) {
+  if (!x || !w || !w2 || !y) return fail(UMIC_ERR_INVALID_ARG, "%s: null pointer", name);
+  if (m < 0 || n < 0 || k <= 0) return fail(UMIC_ERR_INVALID_ARG, "%s: bad sizes", name);
+  if (m > 64) return fail(UMIC_ERR_UNSUPPORTED, "%s: m=%lld > 64 (use umic_gemm)", name,
+                          (long long)m);
+  if (n > 0x7fffffffLL - 16 || k > 0x7fffffffLL - 64)
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: n or k too large", name);
+  if (k % 8 || ldx % 8 || ldw % 8 || !aligned16(x) || !aligned16(w) || !aligned16(w2))
+    return fail(UMIC_ERR_ALIGNMENT, "%s: k, ldx, ldw must be multiples of 8 and x, w 16-byte "
+                "aligned", name);
+  if (ldx < k || ldw < k || ldy < n) return fail(UMIC_ERR_INVALID_ARG, "%s: leading dim", name);
+  return UMIC_OK;
+}
+
+}  // namespace
+}  // namespace umic
+
+using namespace umic;
+
+extern "C" {
+
+int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias, void* y,
+              int64_t ldy, int64_t m, int64_t n, int64_t k, void* stream) {
+  clear_error();
+  if (int rc = check("umic_gemv", x, ldx, w, w, ldw, y, ldy, m, n, k)) return rc;
+  if (m == 0 || n == 0) return UMIC_OK;
+  GemvArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+             nullptr, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
+             ldx, ldw, ldy, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+             static_cast<int>((k + 31) / 32)};
+  return dispatch<false>(a, as_stream(stream));
+}
+
+int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg, const void* wu,
+                            int64_t ldw, void* h, int64_t ldh, int64_t m, int64_t n, int64_t k,
+                            void* stream) {
+  clear_error();
+  if (int rc = check("umic_gemv_gate_silu_mul", x, ldx, wg, wu, ldw, h, ldh, m, n, k)) return rc;
+  if (m == 0 || n == 0) return UMIC_OK;
+  GemvArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(wg),
+             static_cast<const __nv_bfloat16*>(wu), nullptr, static_cast<__nv_bfloat16*>(h),
+             ldx, ldw, ldh, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+             static_cast<int>((k + 31) / 32)};
+  return dispatch<true>(a, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+"""Projections on the B200 kernels: tcgen05 GEMM (umic_gemm) and the decode GEMV (umic_gemv).
+
+`linear(x, weight, bias, act, residual)` mirrors the reference's linear_triton
+(src/umic/kernels/linear.py:118-145): x [M, K] times an nn.Linear weight
+[N, K] without copying it, optional bias, optional GELU epilogue ("gelu" is
+the erf form the reference used; "gelu_tanh" is HF's gelu_pytorch_tanh), plus
+an optional fused residual add. `linear_gemv` is the HBM-bound path for fewer
+than FUSE_MIN_ROWS rows (the reference left those on cuBLAS,
+src/umic/integrate.py:104-105).
+Shapes the kernels reject (N or K not a multiple of 8, misaligned views) go to
+torch's own GPU linear, as the reference leaves unmatched sites on cuBLAS;
+the `stats` counter records every such call.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .. import _lib
+from ._common import require_bf16, require_cuda, row_stride, stats
+
+_ACTS = {None: _lib.EPI_NONE, "gelu": _lib.EPI_GELU_ERF, "gelu_erf": _lib.EPI_GELU_ERF,
+         "gelu_tanh": _lib.EPI_GELU_TANH}
+
+GEMV_MAX_ROWS = 64
+
+
+def _torch_linear(x2d, weight, bias, act, residual):
+    y = F.linear(x2d, weight, bias)
+    if act in ("gelu", "gelu_erf"):
+        y = F.gelu(y)
+    elif act == "gelu_tanh":
+        y = F.gelu(y, approximate="tanh")
+    if residual is not None:
+        y = y + residual
+    return y
+
+
+def _k_major(t: torch.Tensor) -> torch.Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def linear(x2d: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+           act: str | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """y = act(x2d @ weight.T + bias) + residual on the tcgen05 GEMM."""
+    if act not in _ACTS:
+        raise ValueError(f"linear: unsupported act {act!r}")
+    dev = require_cuda("linear", x2d, weight, bias, residual)
+    require_bf16("linear", x2d, weight, bias, residual)
+    m, k = x2d.shape
+    n = weight.shape[0]
+    if weight.shape[1] != k:
+        raise ValueError(f"linear: x has K={k}, weight is {tuple(weight.shape)}")
+    x2d = _k_major(x2d)
+    weight = _k_major(weight)
+    y = torch.empty((m, n), device=x2d.device, dtype=x2d.dtype)
+    if residual is not None and residual.stride(-1) != 1:
+        residual = residual.contiguous()
+    rc = _lib.try_call("umic_gemm", dev, x2d.data_ptr(), row_stride(x2d), weight.data_ptr(),
+                       row_stride(weight), _lib.ptr(bias), _lib.ptr(residual),
+                       row_stride(residual) if residual is not None else 0, y.data_ptr(), n,
+                       m, n, k, _ACTS[act])
+    if rc:
+        stats["linear_fallback"] += 1
+        return _torch_linear(x2d, weight, bias, act, residual)
+    stats["umic_gemm"] += 1
+    return y
+
+
+def linear_gemv(x2d: torch.Tensor, weight: torch.Tensor,
+                bias: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x2d @ weight.T + bias for x2d with fewer than 64 rows (weight-streaming)."""
+    dev = require_cuda("linear_gemv", x2d, weight, bias)
+    require_bf16("linear_gemv", x2d, weight, bias)
+    m, k = x2d.shape
+    n = weight.shape[0]
+    if m > GEMV_MAX_ROWS:
+        raise ValueError(f"linear_gemv: {m} rows > {GEMV_MAX_ROWS}")
+    x2d = _k_major(x2d)
+    weight = _k_major(weight)
+    y = torch.empty((m, n), device=x2d.device, dtype=x2d.dtype)
+    rc = _lib.try_call("umic_gemv", dev, x2d.data_ptr(), row_stride(x2d), weight.data_ptr(),
+                       row_stride(weight), _lib.ptr(bias), y.data_ptr(), n, m, n, k)
+    if rc:
+        stats["gemv_fallback"] += 1
+        return F.linear(x2d, weight, bias)
+    stats["umic_gemv"] += 1
+    return y
+
+
+# Name of the reference interface (src/umic/kernels/linear.py:118).
+linear_triton = linear
