@@ -172,8 +172,9 @@ int dispatch(const GemvArgs& a, cudaStream_t st) {
 
 int check(const char* name, const void* x, int64_t ldx, const void* w, const void* w2,
           int64_t ldw, const void* y, int64_t ldy, int64_t m, int64_t n, int64_t k) {
-  if (!x || !w || !w2 || !y) return fail(UMIC_ERR_INVALID_ARG, "%s: null pointer", name);
   if (m < 0 || n < 0 || k <= 0) return fail(UMIC_ERR_INVALID_ARG, "%s: bad sizes", name);
+  if (m == 0 || n == 0) return UMIC_OK;
+  if (!x || !w || !w2 || !y) return fail(UMIC_ERR_INVALID_ARG, "%s: null pointer", name);
   if (m > 64) return fail(UMIC_ERR_UNSUPPORTED, "%s: m=%lld > 64 (use umic_gemm)", name,
                           (long long)m);
   if (n > 0x7fffffffLL - 16 || k > 0x7fffffffLL - 64)
@@ -196,7 +197,7 @@ int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void
               int64_t ldy, int64_t m, int64_t n, int64_t k, void* stream) {
   clear_error();
   if (int rc = check("umic_gemv", x, ldx, w, w, ldw, y, ldy, m, n, k)) return rc;
-  if (m == 0 || n == 0) return UMIC_OK;
+  if (m == 0 || n == 0) return UMIC_OK;  // nothing to launch
   GemvArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
              nullptr, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
              ldx, ldw, ldy, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),

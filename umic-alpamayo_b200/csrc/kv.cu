@@ -77,11 +77,11 @@ extern "C" int umic_kv_append(void* k_buf, void* v_buf, int64_t buf_sb, int64_t 
                               int64_t n_new, int32_t head_dim, int64_t pos, const int64_t* dpos,
                               void* stream) {
   clear_error();
-  if (!k_buf || !v_buf || !k_new || !v_new)
-    return fail(UMIC_ERR_INVALID_ARG, "umic_kv_append: null pointer");
   if (batch < 0 || heads <= 0 || n_new < 0 || head_dim <= 0 || capacity < 0)
     return fail(UMIC_ERR_INVALID_ARG, "umic_kv_append: bad sizes");
   if (batch == 0 || n_new == 0) return UMIC_OK;
+  if (!k_buf || !v_buf || !k_new || !v_new)
+    return fail(UMIC_ERR_INVALID_ARG, "umic_kv_append: null pointer");
   if (!dpos && (pos < 0 || pos + n_new > capacity))
     return fail(UMIC_ERR_OVERFLOW, "InplaceLayer overflow: pos %lld + new %lld > buffer %lld",
                 (long long)pos, (long long)n_new, (long long)capacity);

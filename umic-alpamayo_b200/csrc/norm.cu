@@ -212,9 +212,10 @@ int dispatch(const NormArgs& a, bool vec_ok, cudaStream_t st) {
 
 int check_common(const char* name, const void* x, const void* w, const void* y, int64_t rows,
                  int64_t n, int w_dtype) {
-  if (!x || !w || !y) return fail(UMIC_ERR_INVALID_ARG, "%s: null pointer", name);
   if (rows < 0 || n <= 0) return fail(UMIC_ERR_INVALID_ARG, "%s: rows=%lld n=%lld", name,
                                       (long long)rows, (long long)n);
+  if (rows == 0) return UMIC_OK;  // empty tensors may carry null data pointers
+  if (!x || !w || !y) return fail(UMIC_ERR_INVALID_ARG, "%s: null pointer", name);
   if (n > 0x7fffffff) return fail(UMIC_ERR_UNSUPPORTED, "%s: n too large", name);
   if (w_dtype != UMIC_DTYPE_BF16 && w_dtype != UMIC_DTYPE_FP32)
     return fail(UMIC_ERR_INVALID_ARG, "%s: bad w_dtype %d", name, w_dtype);
@@ -257,8 +258,8 @@ int umic_add_rmsnorm(const void* x, int64_t sx, const void* r, int64_t sr, const
                      int64_t rows, int64_t n, float eps, void* stream) {
   clear_error();
   if (int rc = check_common("umic_add_rmsnorm", x, w, normed, rows, n, w_dtype)) return rc;
-  if (!r || !summed) return fail(UMIC_ERR_INVALID_ARG, "umic_add_rmsnorm: null pointer");
   if (rows == 0) return UMIC_OK;
+  if (!r || !summed) return fail(UMIC_ERR_INVALID_ARG, "umic_add_rmsnorm: null pointer");
   NormArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(r), w,
              nullptr, static_cast<__nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(summed),
              sx, sr, sn, ss, rows, static_cast<int>(n), w_dtype, eps};
@@ -270,8 +271,8 @@ int umic_layernorm(const void* x, int64_t sx, const void* w, const void* b, int 
                    void* y, int64_t sy, int64_t rows, int64_t n, float eps, void* stream) {
   clear_error();
   if (int rc = check_common("umic_layernorm", x, w, y, rows, n, w_dtype)) return rc;
-  if (!b) return fail(UMIC_ERR_INVALID_ARG, "umic_layernorm: null bias");
   if (rows == 0) return UMIC_OK;
+  if (!b) return fail(UMIC_ERR_INVALID_ARG, "umic_layernorm: null bias");
   NormArgs a{static_cast<const __nv_bfloat16*>(x), nullptr, w, b,
              static_cast<__nv_bfloat16*>(y), nullptr, sx, 0, sy, 0, rows,
              static_cast<int>(n), w_dtype, eps};
@@ -284,8 +285,8 @@ int umic_add_layernorm(const void* x, int64_t sx, const void* r, int64_t sr, con
                        int64_t ss, int64_t rows, int64_t n, float eps, void* stream) {
   clear_error();
   if (int rc = check_common("umic_add_layernorm", x, w, normed, rows, n, w_dtype)) return rc;
-  if (!r || !summed || !b) return fail(UMIC_ERR_INVALID_ARG, "umic_add_layernorm: null pointer");
   if (rows == 0) return UMIC_OK;
+  if (!r || !summed || !b) return fail(UMIC_ERR_INVALID_ARG, "umic_add_layernorm: null pointer");
   NormArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(r), w, b,
              static_cast<__nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(summed), sx, sr,
              sn, ss, rows, static_cast<int>(n), w_dtype, eps};

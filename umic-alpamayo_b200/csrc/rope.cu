@@ -108,11 +108,12 @@ extern "C" int umic_rope_inplace(void* q, int64_t q_sb, int64_t q_ss, int64_t q_
                                  int cos_dtype, int64_t batch, int64_t seq, int32_t head_dim,
                                  void* stream) {
   clear_error();
-  if (!q || !cos || !sin || (hk > 0 && !k))
-    return fail(UMIC_ERR_INVALID_ARG, "umic_rope_inplace: null pointer");
   if (hq <= 0 || hk < 0 || batch < 0 || seq < 0 || head_dim <= 0 || (head_dim & 1))
     return fail(UMIC_ERR_INVALID_ARG, "umic_rope_inplace: hq=%d hk=%d head_dim=%d", hq, hk,
                 head_dim);
+  if (batch == 0 || seq == 0) return UMIC_OK;
+  if (!q || !cos || !sin || (hk > 0 && !k))
+    return fail(UMIC_ERR_INVALID_ARG, "umic_rope_inplace: null pointer");
   if (cos_dtype != UMIC_DTYPE_BF16 && cos_dtype != UMIC_DTYPE_FP32)
     return fail(UMIC_ERR_INVALID_ARG, "umic_rope_inplace: bad cos_dtype %d", cos_dtype);
   if (batch == 0 || seq == 0) return UMIC_OK;
