@@ -13,9 +13,15 @@
 //     the MMA fragments directly (two m16n8k16 steps per 32-wide k slab), with
 //     no shared-memory staging and no bf16->fp32 conversions;
 //   - the warps of a CTA split k into contiguous ranges and meet in shared
-//     memory at the end.
+//     memory at the end;
+//   - small matrices (k/v projections, N = 1024) would leave most SMs idle
+//     with one CTA per 16 rows, so k is also split across a thread-block
+//     cluster of up to 8 CTAs; their partial sums meet in the leader CTA
+//     through distributed shared memory (no global scratch, no atomics).
 // The gated variant streams gate and up rows together and applies
 // silu(g) * u before the single bf16 rounding (fused_ffn.py:86-87 semantics).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace umic {
@@ -51,12 +57,17 @@ __device__ __forceinline__ void slab_mma(float (&c)[4], const uint4& wlo, const 
 
 constexpr int kUnroll = 4;
 
+namespace cg = cooperative_groups;
+
 template <int MC, bool kGated>
-__global__ void __launch_bounds__(512) gemv_kernel(GemvArgs a) {
-  extern __shared__ float red[];  // [warps][kGated+1][MC][4][32]
+__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+  // [warps][kGated+1][MC][4][32] per-warp fragments, then [kGated+1][MC][4][32]
+  // CTA totals (read by the cluster leader).
+  extern __shared__ float red[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int n0 = blockIdx.x * 16;
+  const int csplit = gridDim.y, crank = blockIdx.y;  // k split across the cluster
   const int r0 = n0 + g, r1 = n0 + g + 8;
   const bool r0ok = r0 < a.n, r1ok = r1 < a.n;
 
@@ -70,10 +81,13 @@ __global__ void __launch_bounds__(512) gemv_kernel(GemvArgs a) {
       if constexpr (kGated) acc2[i][j] = 0.f;
     }
 
-  // Contiguous slab range of this warp.
-  const int per = (a.slabs + nwarps - 1) / nwarps;
-  const int s_begin = warp * per;
-  const int s_end = min(a.slabs, s_begin + per);
+  // Contiguous slab range of this CTA, then of this warp.
+  const int per_cta = (a.slabs + csplit - 1) / csplit;
+  const int c_begin = crank * per_cta;
+  const int c_end = min(a.slabs, c_begin + per_cta);
+  const int per = (c_end - c_begin + nwarps - 1) / nwarps;
+  const int s_begin = c_begin + warp * per;
+  const int s_end = min(c_end, s_begin + per);
   const uint4 zero = make_uint4(0, 0, 0, 0);
 
   for (int s0 = s_begin; s0 < s_end; s0 += kUnroll) {
@@ -114,17 +128,34 @@ __global__ void __launch_bounds__(512) gemv_kernel(GemvArgs a) {
       if constexpr (kGated) mine[((MC + mc) * 4 + j) * 32 + lane] = acc2[mc][j];
     }
   __syncthreads();
-  if (warp != 0) return;
   const int stride = kAcc * MC * 4 * 32;
+  float* tot = red + static_cast<size_t>(nwarps) * stride;  // CTA totals
+  for (int i = threadIdx.x; i < stride; i += blockDim.x) {
+    float v = 0.f;
+    for (int w = 0; w < nwarps; ++w) v += red[w * stride + i];
+    tot[i] = v;
+  }
+  if (csplit > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every CTA's totals are in its shared memory
+    if (crank == 0 && warp == 0) {
+      for (int r = 1; r < csplit; ++r) {
+        const float* remote = cluster.map_shared_rank(tot, r);
+        for (int i = lane; i < stride; i += 32) tot[i] += remote[i];
+      }
+    }
+    cluster.sync();  // the leader has read them; peers may exit
+    if (crank != 0) return;
+  } else {
+    __syncthreads();
+  }
+  if (warp != 0) return;
 #pragma unroll
   for (int mc = 0; mc < MC; ++mc) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float v = 0.f, v2 = 0.f;
-      for (int w = 0; w < nwarps; ++w) {
-        v += red[w * stride + (mc * 4 + j) * 32 + lane];
-        if constexpr (kGated) v2 += red[w * stride + ((MC + mc) * 4 + j) * 32 + lane];
-      }
+      const float v = tot[(mc * 4 + j) * 32 + lane];
+      const float v2 = kGated ? tot[((MC + mc) * 4 + j) * 32 + lane] : 0.f;
       // C fragment: c0,c1 -> (row g, cols 2t,2t+1); c2,c3 -> (row g+8, ...)
       const int nrow = (j < 2) ? r0 : r1;
       const int mcol = mc * 8 + 2 * t + (j & 1);
@@ -143,15 +174,34 @@ __global__ void __launch_bounds__(512) gemv_kernel(GemvArgs a) {
 
 template <int MC, bool kGated>
 int launch(const GemvArgs& a, cudaStream_t st) {
-  const int ctas = (a.n + 15) / 16;
-  // Enough warps per SM to keep ~64 KB of weight loads in flight.
-  int warps = (ctas >= 2 * sm_count()) ? 8 : 16;
-  const size_t smem = static_cast<size_t>(warps) * (kGated ? 2 : 1) * MC * 4 * 32 * sizeof(float);
-  static_assert(sizeof(float) == 4, "");
+  const int row_blocks = (a.n + 15) / 16;
+  // Aim for about 4 CTAs per SM; split k over a cluster when the rows alone
+  // give fewer, while keeping at least 4 slabs of 32 per CTA.
+  // Many small work units keep the last wave short (768 row blocks alone are
+  // 1.3 waves of 4 CTAs per SM on 148 SMs).
+  const int target = 16 * sm_count();
+  int csplit = 1;
+  while (csplit < 8 && row_blocks * csplit < target && a.slabs / (csplit * 2) >= 8) csplit *= 2;
+  const int warps = 8;
+  const size_t smem =
+      static_cast<size_t>(warps + 1) * (kGated ? 2 : 1) * MC * 4 * 32 * sizeof(float);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(gemv_kernel<MC, kGated>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-  gemv_kernel<MC, kGated><<<ctas, warps * 32, smem, st>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(row_blocks, csplit, 1);
+  cfg.blockDim = dim3(warps * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = csplit;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<MC, kGated>, a);
+  if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "umic_gemv launch: %s", cudaGetErrorString(e));
   return launch_status("umic_gemv launch");
 }
 

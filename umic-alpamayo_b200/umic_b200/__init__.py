@@ -9,7 +9,8 @@ in libumic_b200.so (C ABI: include/umic_b200.h), called through ctypes.
 
 from . import _lib
 from ._lib import UmicError, device_errors
+from .optimize import UmicConfig, apply
 
 __version__ = "0.1.0"
 
-__all__ = ["UmicError", "device_errors", "__version__"]
+__all__ = ["UmicConfig", "UmicError", "apply", "device_errors", "__version__"]

@@ -49,3 +49,39 @@ def rows_view(x: torch.Tensor) -> tuple[torch.Tensor, int]:
 
 def row_stride(t: torch.Tensor) -> int:
     return t.stride(0) if t.shape[0] > 1 else t.shape[1]
+
+
+# ------------------------------------------------------------ launch probes
+# A benchmark can ask for CUDA events around every launch of a named kernel
+# (recorded on the launching stream) to time that kernel inside a longer step.
+_probes: dict[str, list] = {}
+
+
+def start_probe(name: str) -> None:
+    _probes[name] = []
+
+
+def stop_probe(name: str) -> list[float]:
+    """Stops recording; returns per-launch durations in ms (synchronises)."""
+    evs = _probes.pop(name, [])
+    if evs:
+        evs[-1][1].synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def probe_begin(name: str):
+    lst = _probes.get(name)
+    if lst is None:
+        return None
+    s = torch.cuda.Event(enable_timing=True)
+    s.record()
+    return lst, s
+
+
+def probe_end(token) -> None:
+    if token is None:
+        return
+    lst, s = token
+    e = torch.cuda.Event(enable_timing=True)
+    e.record()
+    lst.append((s, e))

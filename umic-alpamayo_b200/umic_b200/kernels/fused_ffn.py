@@ -15,7 +15,7 @@ import torch
 import torch.nn.functional as F
 
 from .. import _lib
-from ._common import require_bf16, require_cuda, row_stride, stats
+from ._common import probe_begin, probe_end, require_bf16, require_cuda, row_stride, stats
 
 FUSE_MIN_ROWS = 64
 
@@ -52,9 +52,11 @@ def gate_silu_mul_nk(x2d: torch.Tensor, w_gate: torch.Tensor,
                            h.data_ptr(), n, m, n, k)
         name = "umic_gemv_gate_silu_mul"
     else:
+        tok = probe_begin("umic_gemm_gate_silu_mul")
         rc = _lib.try_call("umic_gemm_gate_silu_mul", dev, x2d.data_ptr(), row_stride(x2d),
                            w_gate.data_ptr(), row_stride(w_gate), w_up.data_ptr(),
                            row_stride(w_up), h.data_ptr(), n, m, n, k)
+        probe_end(tok)
         name = "umic_gemm_gate_silu_mul"
     if rc:
         stats["gate_silu_mul_fallback"] += 1
