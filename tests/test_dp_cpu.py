@@ -1,0 +1,73 @@
+"""Episode data parallelism on CPU: sharding, the process launcher with injected
+failures (an exception, a non-zero exit, a hang), and the world-size-2 gloo path
+bench.py uses for its barrier and max-over-ranks timing."""
+
+import multiprocessing as mp
+import socket
+
+import pytest
+
+import dp_workers
+from umic_b200.dp import episode_shard, run_workers
+
+
+@pytest.mark.parametrize("total,world", [(8, 1), (8, 2), (8, 3), (8, 8), (32, 8), (5, 8)])
+def test_shards_cover_every_episode_once(total, world):
+    shards = [episode_shard(total, world, r) for r in range(world)]
+    flat = [e for s in shards for e in s]
+    assert flat == list(range(total))
+    sizes = [len(s) for s in shards]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_launcher_gathers_all_results():
+    res = run_workers(dp_workers.square, 8, 2, timeout_s=120)
+    assert res.ok and sorted(res.results) == list(range(8))
+    assert all(res.results[e]["value"] == e * e for e in range(8))
+    assert {res.results[e]["rank"] for e in range(8)} == {0, 1}
+
+
+def test_exception_on_a_rank_is_reported_and_retried():
+    res = run_workers(dp_workers.fail_on_rank1, 4, 2, timeout_s=120, retries=0)
+    assert not res.ok
+    assert res.failures[0].rank == 1 and "injected failure" in res.failures[0].reason
+    assert res.failures[0].episodes == [2, 3]
+    res = run_workers(dp_workers.fail_on_rank1, 4, 2, timeout_s=120, retries=1)
+    assert sorted(res.results) == [0, 1, 2, 3]
+    assert len(res.history) == 1
+
+
+def test_rank_exit_is_detected():
+    res = run_workers(dp_workers.exit_on_rank0, 4, 2, timeout_s=60)
+    assert [f.rank for f in res.failures] == [0]
+    assert "exit code 3" in res.failures[0].reason
+    assert sorted(res.results) == [2, 3]
+
+
+def test_hung_rank_times_out():
+    res = run_workers(dp_workers.hang_on_rank1, 4, 2, timeout_s=8)
+    assert [f.rank for f in res.failures] == [1]
+    assert "timeout" in res.failures[0].reason
+    assert res.wall_s < 60
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_gloo_world_size_2_barrier_and_max():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=dp_workers.gloo_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # rank 0: episodes 0..3 (sum 6); rank 1: 4..7 (sum 22) + 1 -> max 23 on both
+    assert out[0][1] == out[1][1] == 23.0
+    assert out[0][2] == [[0, 1, 2, 3], [4, 5, 6, 7]]

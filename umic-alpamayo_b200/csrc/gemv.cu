@@ -177,12 +177,14 @@ int launch(const GemvArgs& a, cudaStream_t st) {
   const int row_blocks = (a.n + 15) / 16;
   // Aim for about 4 CTAs per SM; split k over a cluster when the rows alone
   // give fewer, while keeping at least 4 slabs of 32 per CTA.
-  // Many small work units keep the last wave short (768 row blocks alone are
-  // 1.3 waves of 4 CTAs per SM on 148 SMs).
-  const int target = 16 * sm_count();
+  // 4-warp CTAs, about 6 resident per SM: 768 row blocks (a 12288-row matrix)
+  // then fill one wave on 148 SMs instead of spilling a few CTAs into a second
+  // wave. Matrices with fewer row blocks split k across a cluster (up to 8 CTAs,
+  // keeping at least 8 slabs of 32 per CTA).
+  const int target = 5 * sm_count();
   int csplit = 1;
   while (csplit < 8 && row_blocks * csplit < target && a.slabs / (csplit * 2) >= 8) csplit *= 2;
-  const int warps = 8;
+  const int warps = 4;
   const size_t smem =
       static_cast<size_t>(warps + 1) * (kGated ? 2 : 1) * MC * 4 * 32 * sizeof(float);
   if (smem > 48 * 1024)

@@ -112,6 +112,19 @@ def build_vision_model(vision: dict | None = None, device="cuda", seed: int = 3)
     return _finish(model)
 
 
+def tiny_qwen3vl_configs() -> dict:
+    """Tiny Qwen3-VL (text, vision) config pairs for structural-match checks."""
+    rope = {"rope_type": "default", "rope_theta": 1e6, "mrope_section": [2, 3, 3]}
+    t2 = dict(vocab_size=512, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+              num_attention_heads=4, num_key_value_heads=2, head_dim=16, rms_norm_eps=1e-6,
+              rope_parameters=rope)
+    v4 = dict(depth=4, hidden_size=32, intermediate_size=64, num_heads=2, patch_size=14,
+              out_hidden_size=64, num_position_embeddings=64, deepstack_visual_indexes=[1, 2])
+    t3 = dict(t2, num_hidden_layers=3)
+    v2 = dict(v4, depth=2, deepstack_visual_indexes=[0])
+    return {"t2_v4": (t2, v4), "t3_v2": (t3, v2)}
+
+
 class AlpamayoStandIn(nn.Module):
     """Container with Alpamayo's attribute layout: `.vlm` (+ `.expert`)."""
 
