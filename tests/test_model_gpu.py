@@ -1,0 +1,258 @@
+"""Model-level GPU parity of the patched paths (cfg1, cfg3, cfg4, cfg5 shapes).
+
+References: the same HF modules with the same weights run unpatched in fp32
+(an fp32 copy of the model; TF32 off) and in bf16 (the unfused eager GPU path).
+The bar is the north star's: per-tensor max relative error <= 1e-2 against the
+fp32 reference where a few bf16 roundings bound the error (cfg1 block, one
+decoder layer). Deep random-weight stacks (27 ViT blocks, 18 expert layers x 10
+Euler steps) compound bf16 rounding in any implementation -- the unfused bf16
+eager path itself lands at 1.4-2.4e-2 -- so there the fused path must stay as
+close to fp32 as eager does: L2 relative error within 1.1x of eager's and max
+relative error within 1.25x (or under 1e-2).
+"""
+
+import copy
+
+import pytest
+import torch
+
+import oracle
+from umic_b200 import UmicConfig, apply, integrate
+from umic_b200.kernels import stats
+from umic_b200.workloads import (CFG4_TEXT, AlpamayoStandIn, build_vision_model, build_vlm,
+                                 greedy_generate, prefill_ids, vit_inputs)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32_and_unpatch():
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    integrate.unfuse_rope()
+
+
+def _rand(shape, seed, dev, scale=1.0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(dtype).to(dev)
+
+
+def test_cfg1_swiglu_block(cuda):
+    """out = residual' + down(silu(gate(n)) * up(n)), n = RMSNorm(x + residual): the
+    fused path (add_rmsnorm -> dual GEMM -> down GEMM with the residual add in its
+    epilogue) vs the fp32 formula, BASELINE cfg1 sizes and seed."""
+    from types import SimpleNamespace
+
+    m, h, i = 3100, 4096, 12288
+    x = _rand((m, h), 0, cuda)
+    r = _rand((m, h), 1, cuda)
+    w = (1 + 0.05 * _rand((h,), 2, cuda, dtype=torch.float32)).to(torch.bfloat16)
+    wg, wu = _rand((i, h), 3, cuda, 0.02), _rand((i, h), 4, cuda, 0.02)
+    wd = _rand((h, i), 5, cuda, 0.02)
+    mlp = SimpleNamespace(gate_proj=SimpleNamespace(weight=wg, bias=None),
+                          up_proj=SimpleNamespace(weight=wu, bias=None),
+                          down_proj=SimpleNamespace(weight=wd, bias=None))
+    from umic_b200.kernels import add_rmsnorm
+
+    stats.clear()
+    normed, summed = add_rmsnorm(x, r, w, 1e-6)
+    out = integrate.mlp_forward(mlp, normed, residual=summed)
+    assert stats["umic_gemm_gate_silu_mul"] == 1 and stats["umic_gemm"] == 1
+    # fp32 reference on the GPU (same formula as oracle.swiglu_block)
+    s = x.float() + r.float()
+    n = s * torch.rsqrt((s * s).mean(-1, keepdim=True) + 1e-6) * w.float()
+    hh = torch.nn.functional.silu(n @ wg.float().t()) * (n @ wu.float().t())
+    ref = s + hh @ wd.float().t()
+    e = oracle.max_rel_err(out, ref)
+    print(f"cfg1 block max_rel_err={e:.3e} l2={oracle.rel_err(out, ref):.3e}")
+    assert e <= 1e-2
+
+
+def test_cfg1_block_small_vs_cpu_oracle(cuda):
+    m, h, i = 130, 256, 512
+    x, r = _rand((m, h), 10, cuda), _rand((m, h), 11, cuda)
+    w = _rand((h,), 12, cuda)
+    wg, wu, wd = (_rand((i, h), 13, cuda, 0.05), _rand((i, h), 14, cuda, 0.05),
+                  _rand((h, i), 15, cuda, 0.05))
+    from types import SimpleNamespace
+
+    from umic_b200.kernels import add_rmsnorm
+
+    mlp = SimpleNamespace(gate_proj=SimpleNamespace(weight=wg, bias=None),
+                          up_proj=SimpleNamespace(weight=wu, bias=None),
+                          down_proj=SimpleNamespace(weight=wd, bias=None))
+    normed, summed = add_rmsnorm(x, r, w, 1e-6)
+    out = integrate.mlp_forward(mlp, normed, residual=summed)
+    ref = oracle.swiglu_block(x.cpu(), r.cpu(), w.cpu(), 1e-6, wg.cpu(), wu.cpu(), wd.cpu())
+    assert oracle.max_rel_err(out, ref) <= 1e-2
+
+
+def _lm(layers, dev, seed=7, **over):
+    text = dict(CFG4_TEXT, num_hidden_layers=layers, vocab_size=8192, **over)
+    return build_vlm(text=text, device=dev, seed=seed)
+
+
+def test_lm_prefill_hidden_states_vs_fp32(cuda):
+    """Two cfg4-width decoder layers over one 3100-token episode."""
+    vlm = _lm(2, cuda)
+    ids = prefill_ids(1, 3100, vocab=8192, seed=8, device=cuda)
+    ref32 = copy.deepcopy(vlm).float()
+
+    def run(m):
+        with torch.no_grad():
+            out = m.model.language_model(input_ids=ids, output_hidden_states=True)
+        return out.hidden_states[1], out.last_hidden_state
+
+    l1_32, h32 = run(ref32)
+    l1_eager, h_eager = run(vlm)
+    del ref32
+    model = AlpamayoStandIn(vlm)
+    apply(model, UmicConfig(decode_graph=False, decode_cache=False))
+    stats.clear()
+    l1_ours, h_ours = run(vlm)
+    integrate.unfuse_mlps(model)
+    assert stats["umic_gemm_gate_silu_mul"] == 2 and stats["umic_rope_inplace"] == 2
+    e1 = oracle.max_rel_err(l1_ours, l1_32)
+    e_ours, e_eager = oracle.max_rel_err(h_ours, h32), oracle.max_rel_err(h_eager, h32)
+    print(f"prefill layer-1 output: ours {e1:.3e} (eager {oracle.max_rel_err(l1_eager, l1_32):.3e})"
+          f"; 2-layer final: ours {e_ours:.3e}, bf16 eager {e_eager:.3e} (vs fp32)")
+    assert e1 <= 1e-2  # one decoder layer: within the per-tensor bar
+    assert e_ours <= min(5e-2, 1.05 * e_eager)  # the stack: no further from fp32 than eager
+
+
+def _forced_logits(vlm, ids, forced, cache):
+    """Prefill, then one decode step per forced token; returns [B, T+1, V] logits."""
+    with torch.no_grad():
+        out = vlm(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        logits = [out.logits[:, -1].float()]
+        for t in range(forced.shape[1]):
+            out = vlm(input_ids=forced[:, t:t + 1], past_key_values=cache, use_cache=True,
+                      logits_to_keep=1)
+            logits.append(out.logits[:, -1].float())
+    runner = getattr(vlm.forward, "__self__", None)
+    if runner is not None and hasattr(runner, "finish"):
+        runner.finish()
+    return torch.stack(logits, 1)
+
+
+def test_lm_decode_token_stream(cuda):
+    """Prefill + decode through apply() (CUDA-graph decode, in-place KV, GEMV) on a
+    4-layer random-weight decoder. With random weights the top-1 / top-2 logit gaps
+    are often inside bf16 rounding noise, so free-running greedy streams of any two
+    bf16 implementations drift apart; the stream is therefore teacher-forced with
+    the fp32 model's greedy tokens, and the fused path must pick the fp32 argmax at
+    least as often as the unfused bf16 eager path does. Graph replay must be
+    bit-reproducible."""
+    from transformers.cache_utils import DynamicCache
+
+    from umic_b200.workloads import kv_cache_for
+
+    vlm = _lm(4, cuda, hidden_size=1024, intermediate_size=3072, num_attention_heads=8,
+              num_key_value_heads=2, seed=21)
+    ids = prefill_ids(4, 300, vocab=8192, seed=22, device=cuda)
+    ref32 = copy.deepcopy(vlm).float()
+    tok32 = greedy_generate(ref32, ids, 24, cache=DynamicCache())
+    forced = tok32[:, :-1]
+    l32 = _forced_logits(ref32, ids, forced, DynamicCache())
+    del ref32
+    l_eager = _forced_logits(vlm, ids, forced, DynamicCache())
+    model = AlpamayoStandIn(vlm)
+    apply(model, UmicConfig(max_new_tokens=40))
+    try:
+        cache = kv_cache_for(vlm, 4, 300 + 40, cuda)
+        l_ours = _forced_logits(vlm, ids, forced, cache)
+        cache.crop(0)
+        l_ours2 = _forced_logits(vlm, ids, forced, cache)  # pure graph replay
+        got = greedy_generate(vlm, ids, 24, cache=cache)
+        got2 = greedy_generate(vlm, ids, 24, cache=cache)
+    finally:
+        model._umic_decode_runner.release()
+        integrate.unfuse_mlps(model)
+    assert torch.equal(l_ours, l_ours2) and torch.equal(got, got2)
+    a32 = l32.argmax(-1)
+    agree_ours = (l_ours.argmax(-1) == a32).float().mean().item()
+    agree_eager = (l_eager.argmax(-1) == a32).float().mean().item()
+    e_ours, e_eager = oracle.max_rel_err(l_ours, l32), oracle.max_rel_err(l_eager, l32)
+    print(f"teacher-forced top-1 agreement with fp32: ours {agree_ours:.3f}, "
+          f"bf16 eager {agree_eager:.3f}; logits max_rel_err ours {e_ours:.3e}, "
+          f"eager {e_eager:.3e}")
+    assert agree_ours >= agree_eager - 0.02
+    assert e_ours <= max(1e-2, 1.05 * e_eager)
+
+
+@pytest.mark.parametrize("images", [2])
+def test_vit_forward_vs_fp32(cuda, images):
+    """cfg3 ViT (27 blocks, hidden 1280, 16 x 80 heads, tanh-GELU 5120) on 448 x 448
+    images through the fused pipeline (patch-embed GEMM, add+LayerNorm, in-place
+    vision RoPE, packed varlen attention)."""
+    vis = build_vision_model(device=cuda)
+    pix, grid = vit_inputs(images=images, device=cuda)
+    ref32 = copy.deepcopy(vis).float()
+    with torch.no_grad():
+        o32 = ref32(pix.float(), grid_thw=grid)
+        o_eager = vis(pix, grid_thw=grid)
+    del ref32
+    holder = torch.nn.Module()
+    holder.vlm = torch.nn.Module()
+    holder.vlm.visual = vis
+    report = apply(holder, UmicConfig(decode_graph=False, decode_cache=False, decode_gemv=False))
+    assert report["ve_pipeline_fused"] == 1 and report["ve_patch_embed_fused"] == 1
+    stats.clear()
+    with torch.no_grad():
+        o_ours = vis(pix, grid_thw=grid)
+    integrate.unfuse_mlps(holder)
+    assert stats["umic_add_layernorm"] >= 27 and stats["umic_rope_inplace"] == 27
+    for name in ("pooler_output", "last_hidden_state"):
+        a, b, c = getattr(o_ours, name), getattr(o_eager, name), getattr(o32, name)
+        e_ours, e_eager = oracle.max_rel_err(a, c), oracle.max_rel_err(b, c)
+        l2_ours, l2_eager = oracle.rel_err(a, c), oracle.rel_err(b, c)
+        print(f"vit {name} vs fp32: max_rel ours {e_ours:.3e} eager {e_eager:.3e}; "
+              f"l2 ours {l2_ours:.3e} eager {l2_eager:.3e}")
+        assert l2_ours <= max(1e-2, 1.1 * l2_eager)
+        assert e_ours <= max(1e-2, 1.25 * e_eager)
+
+
+def _prefix_cache(layers, episodes, heads, tokens, dim, dev, dtype, seed=30):
+    from transformers.cache_utils import DynamicCache
+
+    g = torch.Generator().manual_seed(seed)
+    c = DynamicCache()
+    for i in range(layers):
+        k = torch.randn(episodes, heads, tokens, dim, generator=g).to(dtype).to(dev)
+        v = torch.randn(episodes, heads, tokens, dim, generator=g).to(dtype).to(dev)
+        c.update(k, v, i)
+    return c
+
+
+def test_flow_expert_euler(cuda):
+    """cfg5: the 18-layer expert (hidden 2048, GQA 16/8 x 128, SwiGLU 8192) runs 10 Euler
+    steps of 64 action tokens per episode over a 3100-token prefix KV that is
+    appended to and cropped back every step. The patched expert (fused MLP / q-o
+    GEMMs, norms, in-place RoPE, in-place KV through the repeat-cache hook) vs fp32."""
+    from umic_b200.workloads import CFG5_EXPERT, build_text_model, flow_sample
+
+    E, T, S = 4, 64, 3100
+    expert = build_text_model(CFG5_EXPERT, device=cuda, seed=5)
+    g = torch.Generator().manual_seed(31)
+    x0 = torch.randn(E, T, 2048, generator=g).to(cuda)
+    ref32 = copy.deepcopy(expert).float()
+    x32 = flow_sample(ref32, _prefix_cache(18, E, 8, S, 128, cuda, torch.float32), S, x0)
+    del ref32
+    x_eager = flow_sample(expert, _prefix_cache(18, E, 8, S, 128, cuda, torch.bfloat16), S,
+                          x0.bfloat16())
+    holder = AlpamayoStandIn(torch.nn.Module(), expert=expert)
+    report = apply(holder, UmicConfig(decode_graph=False, decode_cache=False))
+    assert report["expert_mlp_fused"] == 18 and report["flow_cache_hook"] is True
+    stats.clear()
+    x_ours = flow_sample(expert, _prefix_cache(18, E, 8, S, 128, cuda, torch.bfloat16), S,
+                         x0.bfloat16())
+    integrate.unfuse_mlps(holder)
+    assert stats["umic_gemm_gate_silu_mul"] == 18 * 10 and stats["umic_kv_append"] == 18 * 10
+    e_ours, e_eager = oracle.max_rel_err(x_ours, x32), oracle.max_rel_err(x_eager, x32)
+    l2_ours, l2_eager = oracle.rel_err(x_ours, x32), oracle.rel_err(x_eager, x32)
+    print(f"flow 10 Euler steps vs fp32: max_rel ours {e_ours:.3e} eager {e_eager:.3e}; "
+          f"l2 ours {l2_ours:.3e} eager {l2_eager:.3e}")
+    # 180 layer passes deep: the max-element statistic is noisy, the L2 one is not
+    assert l2_ours <= max(1e-2, 1.1 * l2_eager)
+    assert e_ours <= max(1e-2, 1.25 * e_eager)

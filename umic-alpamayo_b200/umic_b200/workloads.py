@@ -101,7 +101,7 @@ def build_text_model(text: dict | None = None, device="cuda", seed: int = 5) -> 
 
 
 def build_vision_model(vision: dict | None = None, device="cuda", seed: int = 3) -> nn.Module:
-    from transformers import Qwen3VLVisionConfig
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLVisionConfig
     from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLVisionModel
 
     cfg = Qwen3VLVisionConfig(**(vision or CFG3_VISION))
