@@ -41,6 +41,9 @@ TOTAL_EPISODES = 8
 TOKENS = 3100
 LAYERS = 36
 HIDDEN, INTER = 4096, 12288
+# DRAM bytes (read + write) of one dual-GEMM launch at the 8-episode shape
+# (M = 24800), from `ncu --set full` (profiles/gemm_gate_silu_mul_cfg4_prefill.md).
+DUAL_GEMM_TRAFFIC_M24800 = 3.43e9
 
 
 def _peaks() -> dict:
@@ -234,7 +237,9 @@ def run_umic(args) -> None:
     clocks = ClockSampler(vis.split(",")[local] if vis else local)
     clocks.start()
     kc.start_probe("umic_gemm_gate_silu_mul")
+    torch.cuda.nvtx.range_push("umic_timed")  # lets ncu --nvtx-include select this region
     ms_total = timed(step, args.steps)
+    torch.cuda.nvtx.range_pop()
     dur = kc.stop_probe("umic_gemm_gate_silu_mul")
     clk = clocks.stop()
     launches = sum(v for k, v in kc.stats.items() if k.startswith("umic_")) - before
@@ -289,7 +294,10 @@ def run_umic(args) -> None:
                 "frac": achieved / peaks["bf16_tflops_sustained"] if achieved else None,
                 "peak_source": f"{peaks['source']} (sustained: timed inside the step)",
                 "flops_per_launch": flops, "launches": len(dur), "avg_ms": avg_ms,
-                "traffic": args.traffic}
+                "traffic": args.traffic if args.traffic is not None else
+                DUAL_GEMM_TRAFFIC_M24800 * episodes * TOKENS / 24800,
+                "traffic_note": "ncu dram read+write bytes per launch at M=24800, scaled by "
+                                "rows when a rank has fewer episodes"}
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.skip_cpu:

@@ -1,0 +1,77 @@
+"""Single-kernel micro-benchmark of the library against cuBLAS / eager torch.
+
+    python -m umic_b200.kernel_bench [--out results.json]
+
+Each case is timed with CUDA events around one launch after 3 warm-up launches,
+with a 256 MB buffer written between launches to flush L2; the median of 20 is
+reported as (ms, GB/s or TFLOP/s). GEMM cases also report the relative error
+against cuBLAS on the same inputs.
+"""
+import json
+import sys
+
+import torch
+
+from umic_b200.kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inplace,
+                               apply_rotary_vision, gate_silu_mul_nk, linear, linear_gemv)
+
+
+def main() -> None:
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.int8, device=dev)
+
+    def t(fn, iters=20, flushl2=True):
+        for _ in range(3): fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            if flushl2: flush.zero_()
+            s = torch.cuda.Event(enable_timing=True); e = torch.cuda.Event(enable_timing=True)
+            s.record(); fn(); e.record(); torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        ts.sort(); return ts[len(ts)//2]
+
+    res = {}
+    bf = torch.bfloat16
+    x = torch.randn(3100, 4096, device=dev, dtype=bf); r = torch.randn_like(x); w = torch.randn(4096, device=dev, dtype=bf)
+    ms = t(lambda: add_rmsnorm(x, r, w, 1e-6)); res["add_rmsnorm_3100x4096"] = (ms, 101.6e6 / (ms * 1e-3) / 1e9)
+    xv = torch.randn(16384, 1280, device=dev, dtype=bf); rv = torch.randn_like(xv); wv = torch.ones(1280, device=dev, dtype=bf); bv = torch.zeros(1280, device=dev, dtype=bf)
+    ms = t(lambda: add_layernorm(xv, rv, wv, bv, 1e-6)); res["add_layernorm_16384x1280"] = (ms, 16384*1280*2*4 / (ms*1e-3) / 1e9)
+    q = torch.randn(1, 3100, 32, 128, device=dev, dtype=bf).transpose(1, 2); k = torch.randn(1, 3100, 8, 128, device=dev, dtype=bf).transpose(1, 2)
+    cos = torch.randn(1, 3100, 128, device=dev, dtype=bf); sin = torch.randn_like(cos)
+    ms = t(lambda: apply_rotary_text_inplace(q, k, cos, sin)); res["text_rope"] = (ms, 65.1e6/(ms*1e-3)/1e9)
+    qkv = torch.randn(16384, 3, 16, 80, device=dev, dtype=bf); qq, kk, _ = qkv.unbind(1)
+    cv = torch.randn(16384, 80, device=dev); sv = torch.randn_like(cv)
+    ms = t(lambda: apply_rotary_vision(qq, kk, cv, sv)); res["vision_rope_qk"] = (ms, 2*94.4e6/(ms*1e-3)/1e9)
+    for (m, n, kd) in [(3100, 4096, 4096), (24800, 4096, 4096), (8192, 8192, 8192)]:
+        a = torch.randn(m, kd, device=dev, dtype=bf); b = torch.randn(n, kd, device=dev, dtype=bf) * 0.02
+        fl = 2.0 * m * n * kd
+        ms = t(lambda: linear(a, b)); res[f"gemm_{m}x{n}x{kd}"] = (ms, fl / (ms*1e-3) / 1e12)
+        ms = t(lambda: torch.nn.functional.linear(a, b)); res[f"cublas_{m}x{n}x{kd}"] = (ms, fl / (ms*1e-3) / 1e12)
+        err = ((linear(a, b).float() - torch.nn.functional.linear(a, b).float()).norm() / torch.nn.functional.linear(a, b).float().norm()).item()
+        res[f"gemm_{m}x{n}x{kd}_relerr"] = err
+    for m in [3100, 24800]:
+        a = torch.randn(m, 4096, device=dev, dtype=bf); wg = torch.randn(12288, 4096, device=dev, dtype=bf)*0.02; wu = torch.randn_like(wg)
+        fl = 2.0 * 2 * m * 12288 * 4096
+        ms = t(lambda: gate_silu_mul_nk(a, wg, wu)); res[f"dual_{m}"] = (ms, fl/(ms*1e-3)/1e12)
+        ms = t(lambda: torch.nn.functional.silu(torch.nn.functional.linear(a, wg)) * torch.nn.functional.linear(a, wu)); res[f"eager_dual_{m}"] = (ms, fl/(ms*1e-3)/1e12)
+    for (m, n, kd) in [(8, 1024, 4096), (8, 4096, 4096), (8, 4096, 12288), (1, 1024, 4096)]:
+        xs = torch.randn(m, kd, device=dev, dtype=bf); W = torch.randn(n, kd, device=dev, dtype=bf)
+        ms = t(lambda: linear_gemv(xs, W)); res[f"gemv_m{m}_{n}x{kd}"] = (ms, W.numel()*2/(ms*1e-3)/1e9)
+        ms = t(lambda: torch.nn.functional.linear(xs, W)); res[f"cublas_gemv_m{m}_{n}x{kd}"] = (ms, W.numel()*2/(ms*1e-3)/1e9)
+    for m in [1, 8]:
+        xs = torch.randn(m, 4096, device=dev, dtype=bf); W = torch.randn(12288, 4096, device=dev, dtype=bf)
+        ms = t(lambda: linear_gemv(xs, W)); res[f"gemv_m{m}_12288x4096"] = (ms, W.numel()*2/(ms*1e-3)/1e9)
+        ms = t(lambda: torch.nn.functional.linear(xs, W)); res[f"cublas_gemv_m{m}"] = (ms, W.numel()*2/(ms*1e-3)/1e9)
+        W2 = torch.randn(151936, 4096, device=dev, dtype=bf)
+        ms = t(lambda: linear_gemv(xs, W2)); res[f"gemv_m{m}_lmhead"] = (ms, W2.numel()*2/(ms*1e-3)/1e9)
+        del W2
+    for kk_, v in res.items():
+        print(kk_, v)
+    if "--out" in sys.argv:
+        json.dump(res, open(sys.argv[sys.argv.index("--out") + 1], "w"), indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,90 @@
+"""Runs one kernel of the library a few times on a BASELINE shape (profiling driver).
+
+    python -m umic_b200.kernel_driver <mode> [rows] [--iters N]
+
+Used to capture a single kernel under ncu. Modes and shapes:
+  dual           gate/up dual-accumulator GEMM, x [rows=24800, 4096], W [12288, 4096] x 2
+  qo             linear GEMM, x [rows=24800, 4096], W [4096, 4096]
+  add_rmsnorm    [3100, 4096]                  (cfg2a)
+  add_layernorm  [16384, 1280]                 (cfg2b)
+  rope_text      q [3100, 32, 128], k [3100, 8, 128], bf16 tables   (cfg2c)
+  rope_vision    q, k [16384, 16, 80] views of qkv, fp32 tables     (cfg2d)
+  gemv           x [rows=8, 4096], W [12288, 4096]
+  kv             K/V [8, 8, 3100, 128] appended into [8, 8, 3172, 128]
+Inputs are seeded random tensors created on cuda:0 before the launches.
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+
+def make(mode: str, rows: int | None):
+    from .kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inplace,
+                          apply_rotary_vision, gate_silu_mul_nk, kv_append, linear, linear_gemv)
+
+    dev = torch.device("cuda", 0)
+    bf = torch.bfloat16
+    torch.manual_seed(0)
+    if mode == "dual":
+        x = torch.randn(rows or 24800, 4096, device=dev, dtype=bf)
+        wg = torch.randn(12288, 4096, device=dev, dtype=bf) * 0.02
+        wu = torch.randn_like(wg)
+        return lambda: gate_silu_mul_nk(x, wg, wu)
+    if mode == "qo":
+        x = torch.randn(rows or 24800, 4096, device=dev, dtype=bf)
+        w = torch.randn(4096, 4096, device=dev, dtype=bf) * 0.02
+        return lambda: linear(x, w)
+    if mode == "add_rmsnorm":
+        x = torch.randn(3100, 4096, device=dev, dtype=bf)
+        r = torch.randn_like(x)
+        w = torch.randn(4096, device=dev, dtype=bf)
+        return lambda: add_rmsnorm(x, r, w, 1e-6)
+    if mode == "add_layernorm":
+        x = torch.randn(16384, 1280, device=dev, dtype=bf)
+        r = torch.randn_like(x)
+        w = torch.ones(1280, device=dev, dtype=bf)
+        b = torch.zeros_like(w)
+        return lambda: add_layernorm(x, r, w, b, 1e-6)
+    if mode == "rope_text":
+        q = torch.randn(1, 3100, 32, 128, device=dev, dtype=bf).transpose(1, 2)
+        k = torch.randn(1, 3100, 8, 128, device=dev, dtype=bf).transpose(1, 2)
+        c = torch.randn(1, 3100, 128, device=dev, dtype=bf)
+        s = torch.randn_like(c)
+        return lambda: apply_rotary_text_inplace(q, k, c, s)
+    if mode == "rope_vision":
+        qkv = torch.randn(16384, 3, 16, 80, device=dev, dtype=bf)
+        q, k, _ = qkv.unbind(1)
+        c = torch.randn(16384, 80, device=dev)
+        s = torch.randn_like(c)
+        return lambda: apply_rotary_vision(q, k, c, s)
+    if mode == "gemv":
+        x = torch.randn(rows or 8, 4096, device=dev, dtype=bf)
+        w = torch.randn(12288, 4096, device=dev, dtype=bf)
+        return lambda: linear_gemv(x, w)
+    if mode == "kv":
+        kb = torch.zeros(8, 8, 3172, 128, device=dev, dtype=bf)
+        vb = torch.zeros_like(kb)
+        kn = torch.randn(8, 3100, 8, 128, device=dev, dtype=bf).transpose(1, 2)
+        vn = torch.randn_like(kn)
+        return lambda: kv_append(kb, vb, kn, vn, 0)
+    raise SystemExit(f"unknown mode {mode}")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("mode")
+    ap.add_argument("rows", nargs="?", type=int, default=None)
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args()
+    fn = make(a.mode, a.rows)
+    for _ in range(a.iters):
+        fn()
+    torch.cuda.synchronize()
+    print("ok", a.mode)
+
+
+if __name__ == "__main__":
+    main()
