@@ -40,18 +40,29 @@
 namespace umic {
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kBN = 256;  // MMA N (output tile width for linear; 2 x 128 for gate/up)
-constexpr int kBK = 64;   // one 128-byte swizzle atom of bf16
-constexpr int kStages = 4;
+constexpr int kBM = 128;   // accumulator rows per CTA (TMEM lanes)
+constexpr int kBN = 256;   // MMA N (output tile width for linear; 2 x 128 for gate/up)
+constexpr int kBK = 64;    // one 128-byte swizzle atom of bf16
 constexpr int kThreads = 192;
 constexpr int kGroupM = 16;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kABytes = kBM * kBK * 2;       // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;       // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr size_t kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 constexpr long long kWaitLimitCycles = 10000000000LL;
+
+// Per-variant geometry. kPair = 2 runs one MMA over a CTA pair (cta_group::2):
+// the pair computes a 256 x 256 tile, each CTA holding its 128 rows of A and
+// half (128 rows) of B, so a CTA stages 32 KB per k-block instead of 48 KB.
+template <int kPair>
+struct Geo {
+  static constexpr uint32_t kBBytes = kBN * kBK * 2 / kPair;  // B rows held by one CTA
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = kPair == 2 ? 6 : 4;
+  static constexpr size_t kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kTileM = kBM * kPair;
+  // D fp32, A/B bf16, both K-major, N = 256, M = 128 x kPair
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kBN >> 3) << 17) |
+                                     (((kBM * kPair) >> 4) << 24);
+};
 
 struct TcParams {
   __nv_bfloat16* y;
@@ -146,22 +157,70 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: D fp32, A/B bf16, both K-major, N=256, M=128.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kBN >> 3) << 17) |
-                            ((kBM >> 4) << 24);
-
+template <int kPair>
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+  if constexpr (kPair == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(Geo<2>::kIdesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(Geo<1>::kIdesc), "r"(accumulate));
+  }
 }
 
+// Arrive on `bar` (a shared::cluster address, possibly in the peer CTA) once every
+// tcgen05 operation issued so far by this thread has completed.
+template <int kPair>
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
+  if constexpr (kPair == 2) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+  }
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(local), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Remote (or local) arrive on an mbarrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// TMA load of a CTA-pair operand: lands in this CTA's shared memory and counts
+// its bytes on the leader CTA's barrier `bar` (a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t bar, int c0, int c1) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
       : "memory");
 }
 
@@ -205,35 +264,40 @@ __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); 
 
 // ------------------------------------------------------------------ kernel
 
-template <bool kDual>
+template <bool kDual, int kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_b2, TcParams p) {
+  using G = Geo<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kStages * G::kStageBytes);
   // bars: full[kStages], empty[kStages], acc_full[2], acc_empty[2], drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * G::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages);
-  const uint32_t accf0 = smem_u32(bars + 2 * kStages), acce0 = accf0 + 16;
+  const uint32_t rank = kPair == 2 ? cluster_rank() : 0;  // position in the CTA pair
+  const bool leader = rank == 0;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + G::kStages);
+  const uint32_t accf0 = smem_u32(bars + 2 * G::kStages), acce0 = accf0 + 16;
   const uint32_t drain = accf0 + 32;
   const uint32_t sbase = smem_u32(smem);
   const int tiles = p.tiles_m * p.tiles_n;
+  const int unit = kPair == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
+  const int units = kPair == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < G::kStages; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(accf0, 1);
     mbar_init(accf0 + 8, 1);
-    mbar_init(acce0, 128);
-    mbar_init(acce0 + 8, 128);
+    mbar_init(acce0, 128 * kPair);  // every epilogue thread of the pair
+    mbar_init(acce0 + 8, 128 * kPair);
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -243,52 +307,86 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kDual) prefetch_map(&map_b2);
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (kPair == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair == 2) cluster_sync_all();  // peer barriers initialised before any use
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The leader's barriers as seen from either CTA of the pair.
+  const uint32_t lead_full0 = kPair == 2 ? cluster_addr(full0, 0) : full0;
+  const uint32_t lead_acce0 = kPair == 2 ? cluster_addr(acce0, 0) : acce0;
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int issued_stage = -1;
-      bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      bool ok = true, issued = false;
+      for (int t = unit; t < tiles && ok; t += units) {
         int mb, nb;
         tile_coords(t, p, mb, nb);
-        const int row_a = mb * kBM;
-        const int row_b = kDual ? nb * (kBN / 2) : nb * kBN;
+        const int row_a = mb * G::kTileM + static_cast<int>(rank) * kBM;
+        int row_b;
+        const CUtensorMap* bmap = &map_b;
+        if (kDual) {
+          row_b = nb * (kBN / 2);
+          if (kPair == 2 && rank == 1) bmap = &map_b2;  // the pair's second half holds up
+        } else {
+          row_b = nb * kBN + static_cast<int>(rank) * (kBN / kPair);
+        }
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t fb = full0 + 8 * stage;
-          const uint32_t sa = sbase + stage * kStageBytes;
+          const uint32_t sa = sbase + stage * G::kStageBytes;
           const uint32_t sb = sa + kABytes;
-          mbar_expect_tx(fb, kStageBytes);
-          tma_load_2d(sa, &map_a, fb, kb * kBK, row_a);
-          if (kDual) {
-            tma_load_2d(sb, &map_b, fb, kb * kBK, row_b);
-            tma_load_2d(sb + kBBytes / 2, &map_b2, fb, kb * kBK, row_b);
+          if constexpr (kPair == 2) {
+            const uint32_t fb = lead_full0 + 8 * stage;
+            if (leader) mbar_expect_tx(full0 + 8 * stage, 2 * G::kStageBytes);
+            tma_load_2d_pair(sa, &map_a, fb, kb * kBK, row_a);
+            tma_load_2d_pair(sb, bmap, fb, kb * kBK, row_b);
           } else {
-            tma_load_2d(sb, &map_b, fb, kb * kBK, row_b);
+            const uint32_t fb = full0 + 8 * stage;
+            mbar_expect_tx(fb, G::kStageBytes);
+            tma_load_2d(sa, &map_a, fb, kb * kBK, row_a);
+            if (kDual) {
+              tma_load_2d(sb, &map_b, fb, kb * kBK, row_b);
+              tma_load_2d(sb + G::kBBytes / 2, &map_b2, fb, kb * kBK, row_b);
+            } else {
+              tma_load_2d(sb, &map_b, fb, kb * kBK, row_b);
+            }
           }
-          issued_stage = stage;
-          if (++stage == kStages) {
+          issued = true;
+          if (++stage == G::kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      if (!ok && issued_stage >= 0) {
+      if (ok) {
+        // Tail: wait until the MMA has released every stage this CTA filled, so no
+        // commit from the (possibly peer) MMA thread is still in flight at exit.
+        for (int s = 0; s < G::kStages; ++s) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag)) break;
+          if (++stage == G::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      } else if (issued) {
         // Aborting: give the copies already in flight time to land (they take
         // microseconds) before this CTA's shared memory is released.
         const long long t0 = clock64();
@@ -299,12 +397,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+      const uint32_t peer = kPair == 2 ? 1u : 0u;
+      for (int t = unit; t < tiles && ok; t += units, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, p.err, abort_flag)) {
@@ -319,23 +418,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = sbase + stage * kStageBytes;
+          const uint32_t sa = sbase + stage * G::kStageBytes;
           const uint64_t ad = sdesc(sa), bd = sdesc(sa + kABytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             // +32 bytes along K inside the swizzle atom = +2 in the >>4 field
-            mma_bf16(tmem_d, ad + 2 * kk, bd + 2 * kk, (kb | kk) ? 1u : 0u);
+            mma_bf16<kPair>(tmem_d, ad + 2 * kk, bd + 2 * kk, (kb | kk) ? 1u : 0u);
           }
-          mma_commit(empty0 + 8 * stage);
-          if (++stage == kStages) {
+          mma_commit<kPair>(empty0 + 8 * stage);  // frees this stage in both CTAs
+          if (kPair == 2) mma_commit<kPair>(cluster_addr(empty0 + 8 * stage, peer));
+          if (++stage == G::kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
-        if (ok) mma_commit(accf0 + 8 * acc);
+        if (ok) {
+          mma_commit<kPair>(accf0 + 8 * acc);
+          if (kPair == 2) mma_commit<kPair>(cluster_addr(accf0 + 8 * acc, peer));
+        }
       }
       // Wait for every MMA issued by this thread before TMEM is released.
-      mma_commit(drain);
+      mma_commit<kPair>(drain);
       mbar_wait(drain, 0, p.err, abort_flag);
     }
     __syncwarp();
@@ -343,14 +446,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ----------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     int it = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+    for (int t = unit; t < tiles; t += units, ++it) {
       int mb, nb;
       tile_coords(t, p, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(accf0 + 8 * acc, acc_phase, p.err, abort_flag)) break;
       tc_fence_after();
-      const int row = mb * kBM + quarter * 32 + lane;
+      const int row = mb * G::kTileM + static_cast<int>(rank) * kBM + quarter * 32 + lane;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
       constexpr int kOutCols = kDual ? kBN / 2 : kBN;
       const int col0 = nb * kOutCols;
@@ -366,9 +469,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) v[i] = silu(v[i]) * u[i];
         }
         if (c + 32 >= kOutCols) {
-          // All TMEM reads of this tile are done: hand the buffer back.
+          // All TMEM reads of this tile are done: hand the buffer back to the MMA.
           tc_fence_before();
-          mbar_arrive(acce0 + 8 * acc);
+          if (kPair == 2) mbar_arrive_cluster(lead_acce0 + 8 * acc);
+          else mbar_arrive(acce0 + 8 * acc);
         }
         if (row >= p.m) continue;  // rows past m: no stores (TMA read zeros there)
         const int cbase = col0 + c;
@@ -418,11 +522,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  // Neither CTA of a pair leaves (or frees TMEM) while the other may still touch
+  // its barriers or shared memory.
+  if constexpr (kPair == 2) cluster_sync_all();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kTmemCols));
+    if constexpr (kPair == 2) {
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(kTmemCols));
+    } else {
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(kTmemCols));
+    }
   }
 }
 
@@ -464,7 +576,7 @@ bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int64
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool kDual>
+template <bool kDual, int kPair>
 int set_smem_attr() {
   static std::once_flag once[64];
   int dev = 0;
@@ -472,8 +584,9 @@ int set_smem_attr() {
   if (dev < 0 || dev >= 64) dev = 0;
   cudaError_t e = cudaSuccess;
   std::call_once(once[dev], [&] {
-    e = cudaFuncSetAttribute(tc_gemm_kernel<kDual>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes));
+    e = cudaFuncSetAttribute(tc_gemm_kernel<kDual, kPair>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Geo<kPair>::kSmem));
   });
   if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "tc_gemm smem attribute: %s",
                                     cudaGetErrorString(e));
@@ -514,12 +627,13 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
     return fail(UMIC_ERR_INVALID_ARG, "%s: bad epilogue %d", name, epilogue);
 
   const int out_cols = kDual ? kBN / 2 : kBN;
+  // A CTA pair (256-row tiles) whenever there is more than one 128-row block.
+  const bool pair = m > kBM;
+  const int b_rows = pair ? kBN / 2 : (kDual ? kBN / 2 : kBN);
   CUtensorMap ma, mb, mb2;
-  if (!make_map(&ma, x, m, k, ldx, kBM) ||
-      !make_map(&mb, w, n, k, ldw, kDual ? kBN / 2 : kBN) ||
-      !make_map(&mb2, kDual ? w2 : w, n, k, kDual ? ldw2 : ldw, kDual ? kBN / 2 : kBN))
+  if (!make_map(&ma, x, m, k, ldx, kBM) || !make_map(&mb, w, n, k, ldw, b_rows) ||
+      !make_map(&mb2, kDual ? w2 : w, n, k, kDual ? ldw2 : ldw, b_rows))
     return fail(UMIC_ERR_DEVICE, "%s: cuTensorMapEncodeTiled unavailable or rejected", name);
-  if (int rc = set_smem_attr<kDual>()) return rc;
 
   TcParams p;
   p.y = static_cast<__nv_bfloat16*>(y);
@@ -531,15 +645,37 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  p.tiles_m = static_cast<int>((m + kBM - 1) / kBM);
+  const int tile_m = pair ? 2 * kBM : kBM;
+  p.tiles_m = static_cast<int>((m + tile_m - 1) / tile_m);
   p.tiles_n = static_cast<int>((n + out_cols - 1) / out_cols);
   p.kblocks = static_cast<int>((k + kBK - 1) / kBK);
   p.epilogue = epilogue;
   const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x7fffffffLL) return fail(UMIC_ERR_UNSUPPORTED, "%s: too many tiles", name);
   const int sms = sm_count();
-  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  tc_gemm_kernel<kDual><<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(ma, mb, mb2, p);
+  cudaStream_t st = as_stream(stream);
+  if (!pair) {
+    if (int rc = set_smem_attr<kDual, 1>()) return rc;
+    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    tc_gemm_kernel<kDual, 1><<<grid, kThreads, Geo<1>::kSmem, st>>>(ma, mb, mb2, p);
+    return launch_status(name);
+  }
+  if (int rc = set_smem_attr<kDual, 2>()) return rc;
+  const int pairs = static_cast<int>(tiles < sms / 2 ? tiles : sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Geo<2>::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<kDual, 2>, ma, mb, mb2, p);
+  if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", name, cudaGetErrorString(e));
   return launch_status(name);
 }
 
