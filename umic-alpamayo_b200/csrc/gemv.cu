@@ -55,12 +55,13 @@ __device__ __forceinline__ void slab_mma(float (&c)[4], const uint4& wlo, const 
   mma16816(c, wlo.z, whi.z, wlo.w, whi.w, xv.z, xv.w);
 }
 
-constexpr int kUnroll = 4;
-
 namespace cg = cooperative_groups;
 
 template <int MC, bool kGated>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+  // Weight slabs loaded before any math: 8 for the plain small-M case (2 KB of
+  // loads in flight per lane-group of the warp), 4 when registers are scarcer.
+  constexpr int kUnroll = (!kGated && MC <= 2) ? 8 : 4;
   // [warps][kGated+1][MC][4][32] per-warp fragments, then [kGated+1][MC][4][32]
   // CTA totals (read by the cluster leader).
   extern __shared__ float red[];
