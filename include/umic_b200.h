@@ -142,6 +142,27 @@ UMIC_API int umic_kv_append(void* k_buf, void* v_buf, int64_t buf_sb, int64_t bu
                    int64_t n_new, int32_t head_dim, int64_t pos, const int64_t* dpos,
                    void* stream);
 
+/* Attention input in one pass: per-head RMSNorm (weights q_weight / k_weight
+ * [head_dim], eps q_eps / k_eps; NULL weight = no norm) and rotate-half RoPE of q
+ * and k, then the K/V write. q and k are [batch, seq, heads, head_dim] through
+ * their (sb, ss, sh) element strides; v likewise with hk heads. q is rotated in
+ * place. With k_buf != NULL the normalised, rotated k and the unchanged v are
+ * written to the cache buffers [batch, hk, capacity, head_dim] (strides buf_*)
+ * at token position pos (host) or *dpos (device), with the same overflow rules
+ * as umic_kv_append; with k_buf == NULL k is written back in place and v is not
+ * touched. cos/sin as in umic_rope_inplace. head_dim 64, 128 or 256.
+ * Replaces, as one kernel, q_norm / k_norm (_patched_rmsnorm_forward,
+ * integrate.py:134-141), apply_rotary_pos_emb (rope.py:86-107) and the cache
+ * write of InplaceLayer.update (cache.py:59-60, 69-70). */
+UMIC_API int umic_qk_norm_rope_kv(
+    void* q, int64_t q_sb, int64_t q_ss, int64_t q_sh, int32_t hq, void* k, int64_t k_sb,
+    int64_t k_ss, int64_t k_sh, const void* v, int64_t v_sb, int64_t v_ss, int64_t v_sh,
+    int32_t hk, const void* q_weight, const void* k_weight, int w_dtype, float q_eps,
+    float k_eps, const void* cos, const void* sin, int64_t c_sb, int64_t c_ss, int cos_dtype,
+    void* k_buf, void* v_buf, int64_t buf_sb, int64_t buf_sh, int64_t buf_ss, int64_t capacity,
+    int64_t pos, const int64_t* dpos, int64_t batch, int64_t seq, int32_t head_dim,
+    void* stream);
+
 /* ---- projections (src/umic/kernels/linear.py, fused_ffn.py) -------------- */
 
 /* Row-count regime below FUSE_MIN_ROWS (integrate.py:27-30): HBM-bound GEMV,
@@ -150,6 +171,17 @@ UMIC_API int umic_kv_append(void* k_buf, void* v_buf, int64_t buf_sb, int64_t bu
  * (integrate.py:104-105). bias may be NULL. */
 UMIC_API int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
               void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* stream);
+
+/* Up to 3 GEMVs sharing x in one launch (e.g. the q, k and v projections of a
+ * decode step): y_i = x . w_i^T (+ bias_i) for i < count, with w_i [n_i, k],
+ * y_i [m, n_i] (leading dimension ldy_i). Every n_i but the last must be a
+ * multiple of 16. Host arrays of length count; bias may be NULL (or hold NULLs).
+ * No reference counterpart as one call: replaces the q_proj / k_proj / v_proj
+ * calls of one decode step (integrate.py:98-107 and the cuBLAS k/v sites). */
+UMIC_API int umic_gemv_multi(const void* x, int64_t ldx, int32_t count, const void* const* w,
+                             const int64_t* ldw, const int64_t* n, const void* const* bias,
+                             void* const* y, const int64_t* ldy, int64_t m, int64_t k,
+                             void* stream);
 
 /* h[m, n] = silu(x . wg[n]) * (x . wu[n]) for m < 64 rows.
  * Replaces the small-row branch of _fused_mlp_forward (integrate.py:48-50). */

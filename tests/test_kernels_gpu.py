@@ -14,6 +14,8 @@ from umic_b200 import _lib
 from umic_b200.kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inplace,
                                apply_rotary_vision, gate_silu_mul, gate_silu_mul_nk, kv_append,
                                layernorm, linear, linear_gemv, rmsnorm, stats)
+from umic_b200.kernels.attention import qk_norm_rope_kv
+from umic_b200.kernels.linear import linear_gemv_multi
 
 pytestmark = pytest.mark.gpu
 
@@ -169,6 +171,76 @@ def test_kv_append_host_and_device_pos(cuda):
     kv_append(kb, vb, kn, vn, bad)
     assert _lib.device_errors(cuda, clear=True) & _lib.DEVERR_KV_OVERFLOW
     assert torch.equal(kb, snapshot)
+
+
+# ------------------------------------------------- fused attention input
+
+def _qk_ref(x, w, eps, cos, sin):
+    # per-head RMSNorm then rotate-half RoPE, fp32 (oracle formulas); x [B, S, H, D]
+    n = oracle.rmsnorm(x, w, eps)
+    return oracle.rope_rotate_half(n, cos[:, :, None], sin[:, :, None])
+
+
+@pytest.mark.parametrize("batch,seq,hq,hk,d", [(2, 300, 32, 8, 128), (1, 1, 16, 8, 128),
+                                               (3, 5, 4, 2, 64), (1, 7, 2, 1, 256)])
+def test_qk_norm_rope_kv(cuda, batch, seq, hq, hk, d):
+    q = _randn(batch, seq, hq * d, seed=200, dev=cuda).view(batch, seq, hq, d)
+    k = _randn(batch, seq, hk * d, seed=201, dev=cuda).view(batch, seq, hk, d)
+    v = _randn(batch, seq, hk * d, seed=202, dev=cuda).view(batch, seq, hk, d)
+    qw = (1 + 0.1 * _randn(d, seed=203, dev=cuda, dtype=torch.float32)).to(torch.bfloat16)
+    kw = (1 + 0.1 * _randn(d, seed=204, dev=cuda, dtype=torch.float32)).to(torch.bfloat16)
+    pos = torch.arange(seq).unsqueeze(0) + 11 * torch.arange(batch).unsqueeze(1)
+    cs = [oracle.text_rope_cos_sin(p, d, 1e6) for p in pos]
+    cos = torch.stack([c for c, _ in cs]).to(torch.bfloat16).to(cuda)
+    sin = torch.stack([x for _, x in cs]).to(torch.bfloat16).to(cuda)
+    q_ref = _qk_ref(q.cpu(), qw.cpu(), 1e-6, cos.cpu(), sin.cpu())
+    k_ref = _qk_ref(k.cpu(), kw.cpu(), 1e-6, cos.cpu(), sin.cpu())
+    cap, start = seq + 9, 4
+    kb = torch.zeros(batch, hk, cap, d, device=cuda, dtype=torch.bfloat16)
+    vb = torch.zeros_like(kb)
+    q1 = q.clone()
+    stats.clear()
+    qk_norm_rope_kv(q1, k.clone(), v, qw, kw, 1e-6, 1e-6, cos, sin, kb, vb, start)
+    assert stats["umic_qk_norm_rope_kv"] == 1
+    _close(q1, q_ref)
+    _close(kb[:, :, start:start + seq].transpose(1, 2), k_ref)
+    assert torch.equal(vb[:, :, start:start + seq].transpose(1, 2).cpu(), v.cpu())
+    assert int(kb[:, :, :start].count_nonzero()) == 0  # nothing outside the new slots
+    assert int(kb[:, :, start + seq:].count_nonzero()) == 0
+    # without a cache: k rotated in place
+    q2, k2 = q.clone(), k.clone()
+    qk_norm_rope_kv(q2, k2, None, qw, kw, 1e-6, 1e-6, cos, sin)
+    _close(q2, q_ref)
+    _close(k2, k_ref)
+    # device position (graph replay) writes the same bytes
+    if seq == 1:
+        kb2, vb2 = torch.zeros_like(kb), torch.zeros_like(vb)
+        dpos = torch.tensor([start], device=cuda, dtype=torch.int64)
+        qk_norm_rope_kv(q.clone(), k.clone(), v, qw, kw, 1e-6, 1e-6, cos, sin, kb2, vb2, dpos)
+        assert torch.equal(kb2, kb) and torch.equal(vb2, vb)
+
+
+def test_qk_norm_rope_kv_overflow(cuda):
+    q = _randn(1, 4, 2, 128, seed=210, dev=cuda)
+    k = _randn(1, 4, 1, 128, seed=211, dev=cuda)
+    cos = torch.ones(1, 4, 128, device=cuda, dtype=torch.bfloat16)
+    sin = torch.zeros_like(cos)
+    kb = torch.zeros(1, 1, 6, 128, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="overflow"):
+        qk_norm_rope_kv(q, k, k, None, None, 1e-6, 1e-6, cos, sin, kb, kb.clone(), 3)
+
+
+@pytest.mark.parametrize("m", [1, 8, 20])
+def test_gemv_multi_qkv(cuda, m):
+    x = _randn(m, 4096, seed=220, dev=cuda)
+    ws = [_randn(n, 4096, seed=221 + i, dev=cuda, scale=0.02)
+          for i, n in enumerate((4096, 1024, 1000))]
+    bs = [None, _randn(1024, seed=230, dev=cuda), None]
+    stats.clear()
+    outs = linear_gemv_multi(x, ws, bs)
+    assert stats["umic_gemv_multi"] == 1
+    for o, w, b in zip(outs, ws, bs):
+        _close(o, oracle.linear(x.cpu(), w.cpu(), None if b is None else b.cpu()))
 
 
 # ------------------------------------------------------------------ GEMV

@@ -68,6 +68,7 @@ def test_apply_report_and_patching():
         report = apply(model)
         assert report["lm_mlp_fused"] == 2 and report["lm_linear_fused"] == 4
         assert report["lm_rmsnorm_fused"] == 9 and report["lm_add_rmsnorm_fused"] == 2
+        assert report["lm_attention_fused"] == 2
         assert report["text_rope_fused"] is True and report["decode_graph"] is True
         assert report["ve_layernorm_fused"] == 11 and report["ve_pipeline_fused"] == 1
         assert report["ve_patch_embed_fused"] == 1 and report["ve_attn_varlen_fused"] == 4

@@ -112,7 +112,7 @@ def test_lm_prefill_hidden_states_vs_fp32(cuda):
     stats.clear()
     l1_ours, h_ours = run(vlm)
     integrate.unfuse_mlps(model)
-    assert stats["umic_gemm_gate_silu_mul"] == 2 and stats["umic_rope_inplace"] == 2
+    assert stats["umic_gemm_gate_silu_mul"] == 2 and stats["umic_qk_norm_rope_kv"] == 2
     e1 = oracle.max_rel_err(l1_ours, l1_32)
     e_ours, e_eager = oracle.max_rel_err(h_ours, h32), oracle.max_rel_err(h_eager, h32)
     print(f"prefill layer-1 output: ours {e1:.3e} (eager {oracle.max_rel_err(l1_eager, l1_32):.3e})"
@@ -248,7 +248,8 @@ def test_flow_expert_euler(cuda):
     x_ours = flow_sample(expert, _prefix_cache(18, E, 8, S, 128, cuda, torch.bfloat16), S,
                          x0.bfloat16())
     integrate.unfuse_mlps(holder)
-    assert stats["umic_gemm_gate_silu_mul"] == 18 * 10 and stats["umic_kv_append"] == 18 * 10
+    assert stats["umic_gemm_gate_silu_mul"] == 18 * 10
+    assert stats["umic_qk_norm_rope_kv"] == 18 * 10  # KV write fused into the attention prep
     e_ours, e_eager = oracle.max_rel_err(x_ours, x32), oracle.max_rel_err(x_eager, x32)
     l2_ours, l2_eager = oracle.rel_err(x_ours, x32), oracle.rel_err(x_eager, x32)
     print(f"flow 10 Euler steps vs fp32: max_rel ours {e_ours:.3e} eager {e_eager:.3e}; "

@@ -27,15 +27,26 @@
 namespace umic {
 namespace {
 
-struct GemvArgs {
-  const __nv_bfloat16* x;
-  const __nv_bfloat16* w;   // gate when gated
-  const __nv_bfloat16* w2;  // up when gated
+// One weight matrix of a (possibly multi-matrix) launch: rows [row0, row0 + rows)
+// of the concatenated row space are rows [0, rows) of w, written to y.
+struct Seg {
+  const __nv_bfloat16* w;
   const __nv_bfloat16* bias;
   __nv_bfloat16* y;
-  int64_t ldx, ldw, ldy;
-  int m, n, k;
-  int slabs;  // ceil(k / 32)
+  int64_t ldw, ldy;
+  int row0, rows;
+};
+
+constexpr int kMaxSeg = 3;
+
+struct GemvArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w2;  // up weights of the gated variant (segment 0 holds gate)
+  int64_t ldx;
+  Seg seg[kMaxSeg];
+  int nseg;
+  int m, n, k;  // n = total rows over the segments
+  int slabs;    // ceil(k / 32)
 };
 
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -67,10 +78,15 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
   extern __shared__ float red[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int n0 = blockIdx.x * 16;
   const int csplit = gridDim.y, crank = blockIdx.y;  // k split across the cluster
+  // The segment this CTA's 16 rows belong to (boundaries are multiples of 16).
+  int si = 0;
+  while (si + 1 < a.nseg && static_cast<int>(blockIdx.x) * 16 >= a.seg[si + 1].row0) ++si;
+  const Seg sg = a.seg[si];
+  const int n0 = blockIdx.x * 16 - sg.row0;  // first row inside the segment
   const int r0 = n0 + g, r1 = n0 + g + 8;
-  const bool r0ok = r0 < a.n, r1ok = r1 < a.n;
+  const bool r0ok = r0 < sg.rows, r1ok = r1 < sg.rows;
+  const __nv_bfloat16* wp = sg.w;
 
   float acc[MC][4];
   float acc2[kGated ? MC : 1][4];
@@ -97,11 +113,11 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
     for (int u = 0; u < kUnroll; ++u) {
       const int kk = (s0 + u) * 32 + t * 8;
       const bool kok = (s0 + u) < s_end && kk < a.k;
-      wl[u] = (kok && r0ok) ? ld_stream(a.w + r0 * a.ldw + kk) : zero;
-      wh[u] = (kok && r1ok) ? ld_stream(a.w + r1 * a.ldw + kk) : zero;
+      wl[u] = (kok && r0ok) ? ld_stream(wp + r0 * sg.ldw + kk) : zero;
+      wh[u] = (kok && r1ok) ? ld_stream(wp + r1 * sg.ldw + kk) : zero;
       if constexpr (kGated) {
-        ul[u] = (kok && r0ok) ? ld_stream(a.w2 + r0 * a.ldw + kk) : zero;
-        uh[u] = (kok && r1ok) ? ld_stream(a.w2 + r1 * a.ldw + kk) : zero;
+        ul[u] = (kok && r0ok) ? ld_stream(a.w2 + r0 * sg.ldw + kk) : zero;
+        uh[u] = (kok && r1ok) ? ld_stream(a.w2 + r1 * sg.ldw + kk) : zero;
       }
     }
 #pragma unroll
@@ -160,15 +176,15 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
       // C fragment: c0,c1 -> (row g, cols 2t,2t+1); c2,c3 -> (row g+8, ...)
       const int nrow = (j < 2) ? r0 : r1;
       const int mcol = mc * 8 + 2 * t + (j & 1);
-      if (nrow >= a.n || mcol >= a.m) continue;
+      if (nrow >= sg.rows || mcol >= a.m) continue;
       float o;
       if constexpr (kGated) {
         o = v / (1.f + __expf(-v)) * v2;
       } else {
         o = v;
-        if (a.bias) o += bf(a.bias[nrow]);
+        if (sg.bias) o += bf(sg.bias[nrow]);
       }
-      a.y[mcol * a.ldy + nrow] = __float2bfloat16_rn(o);
+      sg.y[mcol * sg.ldy + nrow] = __float2bfloat16_rn(o);
     }
   }
 }
@@ -251,10 +267,49 @@ int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void
   clear_error();
   if (int rc = check("umic_gemv", x, ldx, w, w, ldw, y, ldy, m, n, k)) return rc;
   if (m == 0 || n == 0) return UMIC_OK;  // nothing to launch
-  GemvArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
-             nullptr, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y),
-             ldx, ldw, ldy, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
-             static_cast<int>((k + 31) / 32)};
+  GemvArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.seg[0] = Seg{static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(bias),
+                 static_cast<__nv_bfloat16*>(y), ldw, ldy, 0, static_cast<int>(n)};
+  a.nseg = 1;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.slabs = static_cast<int>((k + 31) / 32);
+  return dispatch<false>(a, as_stream(stream));
+}
+
+int umic_gemv_multi(const void* x, int64_t ldx, int32_t count, const void* const* w,
+                    const int64_t* ldw, const int64_t* n, const void* const* bias,
+                    void* const* y, const int64_t* ldy, int64_t m, int64_t k, void* stream) {
+  clear_error();
+  if (count < 1 || count > kMaxSeg || !w || !ldw || !n || !y || !ldy)
+    return fail(UMIC_ERR_INVALID_ARG, "umic_gemv_multi: count=%d or null array", count);
+  GemvArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  int64_t total = 0;
+  for (int i = 0; i < count; ++i) {
+    if (int rc = check("umic_gemv_multi", x, ldx, w[i], w[i], ldw[i], y[i], ldy[i], m, n[i], k))
+      return rc;
+    if (n[i] <= 0) return fail(UMIC_ERR_INVALID_ARG, "umic_gemv_multi: empty matrix %d", i);
+    if (i + 1 < count && n[i] % 16)
+      return fail(UMIC_ERR_UNSUPPORTED, "umic_gemv_multi: rows of matrix %d not a multiple of 16",
+                  i);
+    a.seg[i] = Seg{static_cast<const __nv_bfloat16*>(w[i]),
+                   bias ? static_cast<const __nv_bfloat16*>(bias[i]) : nullptr,
+                   static_cast<__nv_bfloat16*>(y[i]), ldw[i], ldy[i], static_cast<int>(total),
+                   static_cast<int>(n[i])};
+    total += n[i];
+  }
+  if (m == 0) return UMIC_OK;
+  if (total > 0x7fffffffLL - 16) return fail(UMIC_ERR_UNSUPPORTED, "umic_gemv_multi: too many rows");
+  a.nseg = count;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(total);
+  a.k = static_cast<int>(k);
+  a.slabs = static_cast<int>((k + 31) / 32);
   return dispatch<false>(a, as_stream(stream));
 }
 
@@ -264,10 +319,17 @@ int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg, const vo
   clear_error();
   if (int rc = check("umic_gemv_gate_silu_mul", x, ldx, wg, wu, ldw, h, ldh, m, n, k)) return rc;
   if (m == 0 || n == 0) return UMIC_OK;
-  GemvArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(wg),
-             static_cast<const __nv_bfloat16*>(wu), nullptr, static_cast<__nv_bfloat16*>(h),
-             ldx, ldw, ldh, static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
-             static_cast<int>((k + 31) / 32)};
+  GemvArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.w2 = static_cast<const __nv_bfloat16*>(wu);
+  a.ldx = ldx;
+  a.seg[0] = Seg{static_cast<const __nv_bfloat16*>(wg), nullptr, static_cast<__nv_bfloat16*>(h),
+                 ldw, ldh, 0, static_cast<int>(n)};
+  a.nseg = 1;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.slabs = static_cast<int>((k + 31) / 32);
   return dispatch<true>(a, as_stream(stream));
 }
 

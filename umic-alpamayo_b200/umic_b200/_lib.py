@@ -45,6 +45,13 @@ _SIGNATURES: dict[str, list] = {
     "umic_gemv": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p],
     "umic_gemv_gate_silu_mul": [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64,
                                 _c_i64, _c_p],
+    "umic_gemv_multi": [_c_p, _c_i64, _c_i32, ctypes.POINTER(_c_p), ctypes.POINTER(_c_i64),
+                        ctypes.POINTER(_c_i64), ctypes.POINTER(_c_p), ctypes.POINTER(_c_p),
+                        ctypes.POINTER(_c_i64), _c_i64, _c_i64, _c_p],
+    "umic_qk_norm_rope_kv": [_c_p, _c_i64, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i64, _c_i64,
+                             _c_p, _c_i64, _c_i64, _c_i64, _c_i32, _c_p, _c_p, _c_int, _c_f32,
+                             _c_f32, _c_p, _c_p, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_i64,
+                             _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i32, _c_p],
     "umic_gemm": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64,
                   _c_i64, _c_int, _c_p],
     "umic_gemm_gate_silu_mul": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64,

@@ -64,6 +64,26 @@ class InplaceLayer(DynamicLayer):
         self.values = self._v_buf[:, :, :self._pos, :]
         return self.keys, self.values
 
+    def reserve(self, n: int):
+        """Claims the slots of n new tokens for a kernel that writes K/V itself.
+
+        Returns (k_buf, v_buf, pos): pos is an int, or the device position
+        tensor in graph mode (one token per step). The visible keys /
+        values are advanced exactly as update() would; the caller must write the
+        slots before the attention reads them."""
+        if self.graph_mode and n == 1 and self._pos_t is not None:
+            self.keys = self._k_buf[:, :, :self._graph_len, :]
+            self.values = self._v_buf[:, :, :self._graph_len, :]
+            return self._k_buf, self._v_buf, self._pos_t
+        pos = self._pos
+        if pos + n > self.capacity:
+            raise RuntimeError(f"InplaceLayer overflow: pos {pos} + new {n} > "
+                               f"buffer {self.capacity}")
+        self._pos = pos + n
+        self.keys = self._k_buf[:, :, :self._pos, :]
+        self.values = self._v_buf[:, :, :self._pos, :]
+        return self._k_buf, self._v_buf, pos
+
     def get_seq_length(self, *args, **kwargs) -> int:
         return self._pos
 

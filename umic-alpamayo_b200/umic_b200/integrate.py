@@ -162,6 +162,91 @@ def fuse_decode_linears(model: nn.Module, dry_run: bool = False) -> int:
     return count
 
 
+# --------------------------------------------------------------- attention
+
+def _is_qk_norm_attention(module: nn.Module) -> bool:
+    """q/k/v/o projections plus per-head q_norm / k_norm (Qwen3 text attention)."""
+    for attr in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        if not isinstance(getattr(module, attr, None), nn.Linear):
+            return False
+    for attr in ("q_norm", "k_norm"):
+        w = getattr(getattr(module, attr, None), "weight", None)
+        if not isinstance(w, torch.Tensor) or w.dim() != 1:
+            return False
+    return all(hasattr(module, a) for a in ("head_dim", "scaling", "layer_idx", "config"))
+
+
+def _fused_attention_forward(self, hidden_states, position_embeddings=None, attention_mask=None,
+                             past_key_values=None, **kwargs):
+    """Text attention with its input path fused: projections (one multi-matrix GEMV
+    below FUSE_MIN_ROWS; tcgen05 GEMM for q and the original Linears for k / v above),
+    then one kernel for q_norm / k_norm, RoPE and the KV-cache write, then the
+    model's attention backend and o_proj. Follows HF's Qwen3VLTextAttention.forward;
+    layouts the kernel does not cover run the original forward."""
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import eager_attention_forward
+
+    from .cache import InplaceKVCache
+    from .kernels.attention import qk_norm_rope_kv
+    from .kernels.linear import linear_gemv_multi
+
+    d = self.head_dim
+    cos, sin = position_embeddings if position_embeddings is not None else (None, None)
+    if (cos is None or hidden_states.dim() != 3 or not hidden_states.is_cuda
+            or hidden_states.dtype != torch.bfloat16 or d not in (64, 128, 256)
+            or cos.dim() != 3 or cos.shape[-1] != d or torch.is_grad_enabled()):
+        return type(self).forward(self, hidden_states, position_embeddings, attention_mask,
+                                  past_key_values=past_key_values, **kwargs)
+    b, s, _ = hidden_states.shape
+    x2d = hidden_states.reshape(-1, hidden_states.shape[-1])
+    if x2d.shape[0] < FUSE_MIN_ROWS:
+        q, k, v = linear_gemv_multi(
+            x2d, [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight],
+            [self.q_proj.bias, self.k_proj.bias, self.v_proj.bias])
+    else:
+        q = linear(x2d, self.q_proj.weight, self.q_proj.bias)
+        k = nn.functional.linear(x2d, self.k_proj.weight, self.k_proj.bias)
+        v = nn.functional.linear(x2d, self.v_proj.weight, self.v_proj.bias)
+    q4, k4, v4 = q.view(b, s, -1, d), k.view(b, s, -1, d), v.view(b, s, -1, d)
+    qn, kn = self.q_norm, self.k_norm
+    layer = (past_key_values.layers[self.layer_idx]
+             if isinstance(past_key_values, InplaceKVCache) else None)
+    if layer is not None:
+        kb, vb, pos = layer.reserve(s)
+        qk_norm_rope_kv(q4, k4, v4, qn.weight, kn.weight, _eps_of(qn), _eps_of(kn), cos, sin,
+                        kb, vb, pos)
+        keys, values = layer.keys, layer.values
+    else:
+        qk_norm_rope_kv(q4, k4, None, qn.weight, kn.weight, _eps_of(qn), _eps_of(kn), cos, sin)
+        keys, values = k4.transpose(1, 2), v4.transpose(1, 2)
+        if past_key_values is not None:
+            keys, values = past_key_values.update(keys, values, self.layer_idx)
+    attn = ALL_ATTENTION_FUNCTIONS.get_interface(self.config._attn_implementation,
+                                                 eager_attention_forward)
+    out, weights = attn(self, q4.transpose(1, 2), keys, values, attention_mask,
+                        dropout=0.0 if not self.training else self.attention_dropout,
+                        scaling=self.scaling, **kwargs)
+    out = out.reshape(b, s, -1).contiguous()
+    return self.o_proj(out), weights
+
+
+def fuse_attention(model: nn.Module, dry_run: bool = False) -> int:
+    """Fuse the attention input path (projections, q/k norm, RoPE, KV write) of every
+    Qwen3-style text attention module. No single reference counterpart: it merges the
+    reference's q/o-projection, RMSNorm, text-RoPE and in-place-cache patches
+    (src/umic/integrate.py:98-167, 661-682; src/umic/cache.py:50-80) into one path."""
+    count = 0
+    for _, module in model.named_modules():
+        if not _is_qk_norm_attention(module):
+            continue
+        count += 1
+        if not dry_run:
+            module.forward = _fused_attention_forward.__get__(module)
+    logger.info("fuse_attention: %d module(s) %s", count,
+                "matched (dry run)" if dry_run else "patched")
+    return count
+
+
 # ---------------------------------------------------------------- RMSNorm
 
 def _patched_rmsnorm_forward(self: nn.Module, x: torch.Tensor) -> torch.Tensor:

@@ -1,0 +1,67 @@
+"""Attention-input preparation on the B200 kernel (C ABI: umic_qk_norm_rope_kv).
+
+One launch does what the HF attention forward (transformers qwen3_vl
+Qwen3VLTextAttention.forward) runs as four steps after the projections:
+q_norm / k_norm per head, apply_rotary_pos_emb, and the KV-cache write
+(past_key_values.update -> InplaceLayer.update, src/umic/cache.py:50-80).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from ._common import require_bf16, require_cuda, stats
+from .rmsnorm import _w_dtype
+from .rope import _cos_dtype
+
+
+def qk_norm_rope_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor | None,
+                    q_weight: torch.Tensor | None, k_weight: torch.Tensor | None, q_eps: float,
+                    k_eps: float, cos: torch.Tensor, sin: torch.Tensor, k_buf=None, v_buf=None,
+                    pos: int | torch.Tensor = 0) -> None:
+    """q [B, S, Hq, D] and k / v [B, S, Hk, D] (any strides, D contiguous).
+
+    q is normalised and rotated in place. With k_buf / v_buf ([B, Hk, cap, D]) the
+    normalised, rotated k and v are written at token `pos` (int, or a device int64
+    tensor for graph replay); without them k is rotated in place.
+    """
+    dev = require_cuda("qk_norm_rope_kv", q, k, v, cos, sin, k_buf, v_buf)
+    require_bf16("qk_norm_rope_kv", q, k, v, k_buf, v_buf)
+    b, s, hq, d = q.shape
+    hk = k.shape[2]
+    if k.shape[:2] != (b, s) or k.shape[3] != d:
+        raise ValueError("qk_norm_rope_kv: q / k shapes differ")
+    if cos.shape[-1] != d or cos.stride(-1) != 1 or sin.stride() != cos.stride():
+        raise ValueError("qk_norm_rope_kv: cos/sin must be [B or 1, S, D] with D contiguous")
+    c_sb = cos.stride(0) if cos.shape[0] > 1 else 0
+    if q_weight is not None and k_weight is not None and q_weight.dtype != k_weight.dtype:
+        k_weight = k_weight.to(q_weight.dtype)
+    qw = q_weight.contiguous() if q_weight is not None else None
+    kw = k_weight.contiguous() if k_weight is not None else None
+    wref = qw if qw is not None else kw
+    wdt = _w_dtype(wref) if wref is not None else _lib.DTYPE_BF16
+    if k_buf is not None:
+        if v is None or v_buf is None or v.shape != k.shape:
+            raise ValueError("qk_norm_rope_kv: a cache write needs v and v_buf")
+        cap = k_buf.shape[2]
+        bs = (k_buf.stride(0), k_buf.stride(1), k_buf.stride(2))
+        if isinstance(pos, torch.Tensor):
+            host_pos, dpos = 0, pos.data_ptr()
+        else:
+            host_pos, dpos = int(pos), None
+    else:
+        cap, bs, host_pos, dpos = 0, (0, 0, 0), 0, None
+    vs = (v.stride(0), v.stride(1), v.stride(2)) if v is not None else (0, 0, 0)
+    try:
+        _lib.call("umic_qk_norm_rope_kv", dev, q.data_ptr(), q.stride(0), q.stride(1),
+                  q.stride(2), hq, k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+                  _lib.ptr(v), vs[0], vs[1], vs[2], hk, _lib.ptr(qw), _lib.ptr(kw), wdt,
+                  float(q_eps), float(k_eps), cos.data_ptr(), sin.data_ptr(), c_sb,
+                  cos.stride(1), _cos_dtype(cos), _lib.ptr(k_buf), _lib.ptr(v_buf), bs[0],
+                  bs[1], bs[2], cap, host_pos, dpos, b, s, d)
+    except _lib.UmicError as e:
+        if e.code == _lib.ERR_OVERFLOW:
+            raise RuntimeError(str(e).split(": ", 1)[-1]) from None
+        raise
+    stats["umic_qk_norm_rope_kv"] += 1

@@ -89,5 +89,34 @@ def linear_gemv(x2d: torch.Tensor, weight: torch.Tensor,
     return y
 
 
+def linear_gemv_multi(x2d: torch.Tensor, weights: list[torch.Tensor],
+                      biases: list[torch.Tensor | None] | None = None) -> list[torch.Tensor]:
+    """[x2d @ w.T + b for each w] in one launch (x2d with fewer than 64 rows); used for
+    the q/k/v projections of a decode step."""
+    import ctypes
+
+    dev = require_cuda("linear_gemv_multi", x2d, *weights)
+    require_bf16("linear_gemv_multi", x2d, *weights)
+    m, k = x2d.shape
+    cnt = len(weights)
+    biases = biases or [None] * cnt
+    if m > GEMV_MAX_ROWS or not 1 <= cnt <= 3 or any(w.shape[1] != k for w in weights):
+        raise ValueError("linear_gemv_multi: bad shapes")
+    x2d = _k_major(x2d)
+    weights = [_k_major(w) for w in weights]
+    outs = [torch.empty((m, w.shape[0]), device=x2d.device, dtype=x2d.dtype) for w in weights]
+    P = ctypes.c_void_p * cnt
+    I = ctypes.c_int64 * cnt
+    rc = _lib.try_call("umic_gemv_multi", dev, x2d.data_ptr(), row_stride(x2d), cnt,
+                       P(*[w.data_ptr() for w in weights]), I(*[row_stride(w) for w in weights]),
+                       I(*[w.shape[0] for w in weights]), P(*[_lib.ptr(b) for b in biases]),
+                       P(*[o.data_ptr() for o in outs]), I(*[o.shape[1] for o in outs]), m, k)
+    if rc:
+        stats["gemv_fallback"] += 1
+        return [F.linear(x2d, w, b) for w, b in zip(weights, biases)]
+    stats["umic_gemv_multi"] += 1
+    return outs
+
+
 # Name of the reference interface (src/umic/kernels/linear.py:118).
 linear_triton = linear

@@ -2,10 +2,13 @@
 
 Mirrors src/umic/optimize.py of soonhong99/umic-alpamayo: same UmicConfig
 fields and defaults, same report keys, same order of patches, and the same
-rule that a model where nothing matches is left unchanged (no error). Two
-additions, both on by default and both reported:
+rule that a model where nothing matches is left unchanged (no error).
+Additions, on by default and reported:
+  * attention_fusion: the text attention input path (projections, per-head
+    q/k RMSNorm, RoPE, KV-cache write) runs as one kernel after the projections;
   * decode_gemv: every remaining LM / expert Linear runs the GEMV kernel when
     it sees fewer than FUSE_MIN_ROWS rows (the reference left those on cuBLAS);
+  * the expert's MLPs and q/o projections take the same GEMMs as the LM;
   * the LM / expert lookups also accept the transformers 5.x layout, where the
     VLM holds its language model and vision tower under `.model`.
 """
@@ -37,6 +40,7 @@ class UmicConfig:
     adaptive_flow: bool = False
     max_new_tokens: int = 96
     decode_gemv: bool = True
+    attention_fusion: bool = True
 
 
 def _has_layers(m) -> bool:
@@ -92,6 +96,8 @@ def apply(model: nn.Module, config: UmicConfig | None = None) -> dict:
             report["lm_rmsnorm_fused"] = integrate.fuse_rmsnorms(lm)
         if cfg.add_rmsnorm_fusion:
             report["lm_add_rmsnorm_fused"] = integrate.fuse_add_rmsnorm(lm)
+        if cfg.attention_fusion:
+            report["lm_attention_fused"] = integrate.fuse_attention(lm)
 
     if cfg.text_rope_fusion:
         report["text_rope_fused"] = integrate.fuse_text_rope()
@@ -114,6 +120,8 @@ def apply(model: nn.Module, config: UmicConfig | None = None) -> dict:
             report["expert_mlp_fused"] = integrate.fuse_mlps(expert)
         if cfg.linear_fusion:
             report["expert_linear_fused"] = integrate.fuse_linears(expert)
+        if cfg.attention_fusion:
+            report["expert_attention_fused"] = integrate.fuse_attention(expert)
     if cfg.flow_cache and expert is not None:
         integrate.fuse_repeat_cache(expert)
         report["flow_cache_hook"] = True
