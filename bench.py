@@ -268,18 +268,23 @@ def run_umic(args) -> None:
             e = torch.cuda.Event(enable_timing=True)
             s.record()
             toks = [t]
-            for _ in range(n_decode):
-                out = vlm(input_ids=t[:, None], past_key_values=cache, use_cache=True,
-                          logits_to_keep=1)
-                t = out.logits[:, -1].argmax(-1)
-                toks.append(t)
+            with torch.no_grad():
+                for _ in range(n_decode):
+                    out = vlm(input_ids=t[:, None], past_key_values=cache, use_cache=True,
+                              logits_to_keep=1)
+                    t = out.logits[:, -1].argmax(-1)
+                    toks.append(t)
             e.record()
             torch.cuda.synchronize()
             model._umic_decode_runner.finish()
             return s.elapsed_time(e), torch.stack(toks, 1)
 
-        decode_run()  # captures one graph per KV length
-        dms, toks = decode_run()  # replay
+        # The first pass runs the runner's eager warm-up steps and captures the graphs of
+        # the remaining KV lengths; the second captures the warm-up lengths; the third
+        # replays every step.
+        decode_run()
+        decode_run()
+        dms, toks = decode_run()
         dms = max_over_ranks(dms)
         decode = {"steps": n_decode, "ms_per_step": dms / n_decode,
                   "tokens_per_s": TOTAL_EPISODES * n_decode

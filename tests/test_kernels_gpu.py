@@ -181,18 +181,21 @@ def _qk_ref(x, w, eps, cos, sin):
     return oracle.rope_rotate_half(n, cos[:, :, None], sin[:, :, None])
 
 
-@pytest.mark.parametrize("batch,seq,hq,hk,d", [(2, 300, 32, 8, 128), (1, 1, 16, 8, 128),
-                                               (3, 5, 4, 2, 64), (1, 7, 2, 1, 256)])
-def test_qk_norm_rope_kv(cuda, batch, seq, hq, hk, d):
+@pytest.mark.parametrize("batch,seq,hq,hk,d,tdt", [
+    (2, 300, 32, 8, 128, torch.bfloat16), (1, 1, 16, 8, 128, torch.bfloat16),
+    (3, 5, 4, 2, 64, torch.bfloat16), (1, 7, 2, 1, 256, torch.bfloat16),
+    (2, 9, 6, 3, 128, torch.float32), (1, 3, 40, 40, 64, torch.float32)])
+def test_qk_norm_rope_kv(cuda, batch, seq, hq, hk, d, tdt):
+    """tdt: dtype of the cos / sin tables and the per-head norm weights."""
     q = _randn(batch, seq, hq * d, seed=200, dev=cuda).view(batch, seq, hq, d)
     k = _randn(batch, seq, hk * d, seed=201, dev=cuda).view(batch, seq, hk, d)
     v = _randn(batch, seq, hk * d, seed=202, dev=cuda).view(batch, seq, hk, d)
-    qw = (1 + 0.1 * _randn(d, seed=203, dev=cuda, dtype=torch.float32)).to(torch.bfloat16)
-    kw = (1 + 0.1 * _randn(d, seed=204, dev=cuda, dtype=torch.float32)).to(torch.bfloat16)
+    qw = (1 + 0.1 * _randn(d, seed=203, dev=cuda, dtype=torch.float32)).to(tdt)
+    kw = (1 + 0.1 * _randn(d, seed=204, dev=cuda, dtype=torch.float32)).to(tdt)
     pos = torch.arange(seq).unsqueeze(0) + 11 * torch.arange(batch).unsqueeze(1)
     cs = [oracle.text_rope_cos_sin(p, d, 1e6) for p in pos]
-    cos = torch.stack([c for c, _ in cs]).to(torch.bfloat16).to(cuda)
-    sin = torch.stack([x for _, x in cs]).to(torch.bfloat16).to(cuda)
+    cos = torch.stack([c for c, _ in cs]).to(tdt).to(cuda)
+    sin = torch.stack([x for _, x in cs]).to(tdt).to(cuda)
     q_ref = _qk_ref(q.cpu(), qw.cpu(), 1e-6, cos.cpu(), sin.cpu())
     k_ref = _qk_ref(k.cpu(), kw.cpu(), 1e-6, cos.cpu(), sin.cpu())
     cap, start = seq + 9, 4

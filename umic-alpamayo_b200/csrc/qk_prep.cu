@@ -5,14 +5,14 @@
 // launch each, src/umic/integrate.py:134-141 applied to the per-head norms),
 // apply_rotary_pos_emb (src/umic/kernels/rope.py:86-107) and the cache write
 // (src/umic/cache.py:59-60, 69-70) -- each reading and writing q/k through HBM.
-// Here a group of D/8 threads owns one head row of one token (8 consecutive
-// elements per thread, 16-byte loads): the sum of squares is reduced with
-// shuffles inside the group, the normalised values stay in registers, and the
-// RoPE partner (element d +/- D/2) is held by the thread D/16 lanes away, so one
-// shuffle brings it over. q is written back in place; k (normalised, rotated)
-// and v (copied) go straight to [b, h, pos + s, :] of the cache buffers, or k is
-// written back in place when no cache buffer is given. Math in fp32, one bf16
-// rounding per output.
+// Here a group of D/16 threads owns one head row of one token; each thread holds
+// 8 elements of the first half (d0 = 8 * lane) and their 8 rotate-half partners
+// (d0 + D/2), two 16-byte loads. The sum of squares is reduced with log2(D/16)
+// shuffles, the normalised values stay in registers and the RoPE partner is
+// already in the same thread, so the rotation needs no data exchange. q is
+// written back in place; k (normalised, rotated) and v (copied) go straight to
+// [b, h, pos + s, :] of the cache buffers, or k is written back in place when no
+// cache buffer is given. Math in fp32, one bf16 rounding per output.
 #include "common.cuh"
 
 namespace umic {
@@ -40,13 +40,12 @@ struct PrepArgs {
   int64_t seq;
   int hq, hk;
   int w_dtype;
-  int cos_fp32;
   float q_eps, k_eps;
 };
 
-__device__ __forceinline__ void load_table8(const void* base, bool fp32, int64_t idx,
-                                            float (&f)[8]) {
-  if (fp32) {
+template <bool kFp32>
+__device__ __forceinline__ void load_table8(const void* base, int64_t idx, float (&f)[8]) {
+  if constexpr (kFp32) {
     const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + idx);
     const float4 a = __ldg(p), b = __ldg(p + 1);
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
@@ -56,13 +55,17 @@ __device__ __forceinline__ void load_table8(const void* base, bool fp32, int64_t
   }
 }
 
-// block = 256 threads = 256 / TPH head rows of one token; grid = (seq, batch,
-// ceil(rows / rows per block)). Row index r: [0, hq) q heads, [hq, hq+hk) k heads,
-// then [hq+hk, hq+2hk) v heads when the K/V go to a cache.
-template <int TPH>
-__global__ void __launch_bounds__(256) qk_prep_kernel(PrepArgs a) {
-  constexpr int kRowsPerBlock = 256 / TPH;
-  constexpr int kHalf = TPH / 2;  // partner lane distance (D/16 threads)
+constexpr int kPrepThreads = 128;
+
+// block = 128 threads = 128 / TPH head rows of one token, TPH = D / 16; grid =
+// (seq, batch, ceil(rows / rows per block)). Row index r: [0, hq) q heads,
+// [hq, hq+hk) k heads, then [hq+hk, hq+2hk) v heads when the K/V go to a cache.
+// One token per thread with a small register footprint keeps many blocks resident,
+// which is what bounds this kernel (the work per byte is a few dozen instructions).
+template <int TPH, bool kCosFp32>
+__global__ void __launch_bounds__(kPrepThreads) qk_prep_kernel(PrepArgs a) {
+  constexpr int kRowsPerBlock = kPrepThreads / TPH;
+  constexpr int kHalfD = TPH * 8;  // D / 2
   const int sub = threadIdx.x % TPH;
   const int r = blockIdx.z * kRowsPerBlock + threadIdx.x / TPH;
   const int64_t s = blockIdx.x, b = blockIdx.y;
@@ -78,62 +81,79 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(PrepArgs a) {
     }
   }
   const int d0 = sub * 8;
-  float x[8];
-  // v rows: plain copy into the cache (no norm, no rotation)
-  const bool is_v = active && r >= a.hq + a.hk;
-  if (is_v) {
-    const int h = r - a.hq - a.hk;
-    const uint4 val = ld_stream(a.v + b * a.v_sb + s * a.v_ss + h * a.v_sh + d0);
-    if (a.kb) st_vec(a.vb + b * a.b_sb + h * a.b_sh + (pos + s) * a.b_ss + d0, val);
-  }
   const bool is_q = active && r < a.hq;
+  const bool is_v = active && r >= a.hq + a.hk;
   const bool is_k = active && !is_q && !is_v;
-  __nv_bfloat16* src = nullptr;
-  if (is_q) src = a.q + b * a.q_sb + s * a.q_ss + r * a.q_sh;
-  else if (is_k) src = a.k + b * a.k_sb + s * a.k_ss + (r - a.hq) * a.k_sh;
-  if (src) unpack8(ld_stream(src + d0), x);
-  else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[j] = 0.f;
+  const __nv_bfloat16* src = nullptr;
+  __nv_bfloat16* dst = nullptr;
+  if (is_q) {
+    dst = a.q + b * a.q_sb + s * a.q_ss + r * a.q_sh + d0;
+    src = dst;
+  } else if (is_k) {
+    const int h = r - a.hq;
+    dst = a.k + b * a.k_sb + s * a.k_ss + h * a.k_sh + d0;
+    src = dst;
+    if (a.kb) dst = a.kb + b * a.b_sb + h * a.b_sh + (pos + s) * a.b_ss + d0;
+  } else if (is_v) {
+    const int h = r - a.hq - a.hk;
+    src = a.v + b * a.v_sb + s * a.v_ss + h * a.v_sh + d0;
+    dst = a.vb + b * a.b_sb + h * a.b_sh + (pos + s) * a.b_ss + d0;
   }
-  // per-head RMSNorm (all lanes of the group take part in the shuffles)
-  const void* w = is_q ? a.qw : a.kw;
+  uint4 xa = make_uint4(0, 0, 0, 0), xb = xa;
+  if (src) {
+    xa = ld_stream(src);
+    xb = ld_stream(src + kHalfD);
+  }
+  if (is_v) {  // v rows: plain copy into the cache (no norm, no rotation)
+    st_vec(dst, xa);
+    st_vec(dst + kHalfD, xb);
+  }
+  float x[8], y[8];
+  unpack8(xa, x);
+  unpack8(xb, y);
+  // per-head RMSNorm: all lanes of the group take part in the shuffles
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
 #pragma unroll
+  for (int j = 0; j < 8; ++j) ss += y[j] * y[j];
+#pragma unroll
   for (int o = TPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (w && src) {
-    const float rstd = rsqrtf(ss / static_cast<float>(TPH * 8) + (is_q ? a.q_eps : a.k_eps));
+  if (!is_q && !is_k) return;
+  const void* w = is_q ? a.qw : a.kw;
+  if (w) {
+    const float rstd = rsqrtf(ss / static_cast<float>(TPH * 16) + (is_q ? a.q_eps : a.k_eps));
     float wv[8];
     load_w8(w, a.w_dtype, d0, wv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) x[j] = x[j] * rstd * wv[j];
-  }
-  // rotate-half RoPE: lanes sub < kHalf hold the first half, their partners sub + kHalf
-  float p[8];
+    load_w8(w, a.w_dtype, d0 + kHalfD, wv);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) p[j] = __shfl_xor_sync(0xffffffffu, x[j], kHalf);
-  if (!src) return;
-  const int64_t crow = b * a.c_sb + s * a.c_ss;
-  float c[8], sn[8];
-  load_table8(a.cos, a.cos_fp32, crow + d0, c);
-  load_table8(a.sin, a.cos_fp32, crow + d0, sn);
-  float o[8];
-  if (sub < kHalf) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = x[j] * c[j] - p[j] * sn[j];
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = x[j] * c[j] + p[j] * sn[j];
+    for (int j = 0; j < 8; ++j) y[j] = y[j] * rstd * wv[j];
   }
-  const uint4 out = pack8(o);
-  if (is_q || !a.kb) {
-    st_vec(src + d0, out);
-  } else {
-    const int h = r - a.hq;
-    st_vec(a.kb + b * a.b_sb + h * a.b_sh + (pos + s) * a.b_ss + d0, out);
-  }
+  // rotate-half RoPE: out[d] = x[d] cos[d] - x[d + D/2] sin[d] for the first half,
+  // out[d + D/2] = x[d + D/2] cos[d + D/2] + x[d] sin[d + D/2] for the second
+  const int64_t crow = b * a.c_sb + s * a.c_ss + d0;
+  float c[8], sn[8], o[8];
+  load_table8<kCosFp32>(a.cos, crow, c);
+  load_table8<kCosFp32>(a.sin, crow, sn);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = x[j] * c[j] - y[j] * sn[j];
+  st_vec(dst, pack8(o));
+  load_table8<kCosFp32>(a.cos, crow + kHalfD, c);
+  load_table8<kCosFp32>(a.sin, crow + kHalfD, sn);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = y[j] * c[j] + x[j] * sn[j];
+  st_vec(dst + kHalfD, pack8(o));
+}
+
+template <int TPH>
+void launch_prep(const PrepArgs& a, int64_t seq, int64_t batch, int zblocks, bool cos32,
+                 cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>(seq), static_cast<unsigned>(batch),
+                  static_cast<unsigned>(zblocks));
+  if (cos32) qk_prep_kernel<TPH, true><<<grid, kPrepThreads, 0, st>>>(a);
+  else qk_prep_kernel<TPH, false><<<grid, kPrepThreads, 0, st>>>(a);
 }
 
 }  // namespace
@@ -187,16 +207,18 @@ extern "C" int umic_qk_norm_rope_kv(
              static_cast<const __nv_bfloat16*>(v), q_weight, k_weight, cos, sin,
              static_cast<__nv_bfloat16*>(k_buf), static_cast<__nv_bfloat16*>(v_buf), dpos,
              device_error_word(), q_sb, q_ss, q_sh, k_sb, k_ss, k_sh, v_sb, v_ss, v_sh, c_sb,
-             c_ss, buf_sb, buf_sh, buf_ss, capacity, pos, seq, hq, hk, w_dtype,
-             cos_dtype == UMIC_DTYPE_FP32 ? 1 : 0, q_eps, k_eps};
-  const int tph = head_dim / 8;
-  const int rows_per_block = 256 / tph;
+             c_ss, buf_sb, buf_sh, buf_ss, capacity, pos, seq, hq, hk, w_dtype, q_eps,
+             k_eps};
+  const int tph = head_dim / 16;
+  const int rows_per_block = kPrepThreads / tph;
   const int rows = hq + (k_buf ? 2 * hk : hk);
-  const dim3 grid(static_cast<unsigned>(seq), static_cast<unsigned>(batch),
-                  static_cast<unsigned>((rows + rows_per_block - 1) / rows_per_block));
+  const int zblocks = (rows + rows_per_block - 1) / rows_per_block;
+  if (zblocks > 65535)
+    return fail(UMIC_ERR_UNSUPPORTED, "umic_qk_norm_rope_kv: too many heads (%d + %d)", hq, hk);
+  const bool cos32 = cos_dtype == UMIC_DTYPE_FP32;
   cudaStream_t st = as_stream(stream);
-  if (tph == 8) qk_prep_kernel<8><<<grid, 256, 0, st>>>(a);
-  else if (tph == 16) qk_prep_kernel<16><<<grid, 256, 0, st>>>(a);
-  else qk_prep_kernel<32><<<grid, 256, 0, st>>>(a);
+  if (tph == 4) launch_prep<4>(a, seq, batch, zblocks, cos32, st);
+  else if (tph == 8) launch_prep<8>(a, seq, batch, zblocks, cos32, st);
+  else launch_prep<16>(a, seq, batch, zblocks, cos32, st);
   return launch_status("umic_qk_norm_rope_kv");
 }

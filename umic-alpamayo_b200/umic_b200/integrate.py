@@ -194,7 +194,9 @@ def _fused_attention_forward(self, hidden_states, position_embeddings=None, atte
     cos, sin = position_embeddings if position_embeddings is not None else (None, None)
     if (cos is None or hidden_states.dim() != 3 or not hidden_states.is_cuda
             or hidden_states.dtype != torch.bfloat16 or d not in (64, 128, 256)
-            or cos.dim() != 3 or cos.shape[-1] != d or torch.is_grad_enabled()):
+            or cos.dim() != 3 or cos.shape[-1] != d
+            or (torch.is_grad_enabled()
+                and (hidden_states.requires_grad or self.q_proj.weight.requires_grad))):
         return type(self).forward(self, hidden_states, position_embeddings, attention_mask,
                                   past_key_values=past_key_values, **kwargs)
     b, s, _ = hidden_states.shape
