@@ -5,6 +5,8 @@
 Used to capture a single kernel under ncu. Modes and shapes:
   dual           gate/up dual-accumulator GEMM, x [rows=24800, 4096], W [12288, 4096] x 2
   qo             linear GEMM, x [rows=24800, 4096], W [4096, 4096]
+  qo_cublas      the same shape through torch (cuBLAS), for side-by-side counters
+  qk_prep        q/k RMSNorm + RoPE + K/V cache write, [rows=8 episodes, 3100, 32/8, 128]
   add_rmsnorm    [3100, 4096]                  (cfg2a)
   add_layernorm  [16384, 1280]                 (cfg2b)
   rope_text      q [3100, 32, 128], k [3100, 8, 128], bf16 tables   (cfg2c)
@@ -24,6 +26,7 @@ import torch
 def make(mode: str, rows: int | None):
     from .kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inplace,
                           apply_rotary_vision, gate_silu_mul_nk, kv_append, linear, linear_gemv)
+    from .kernels.attention import qk_norm_rope_kv
 
     dev = torch.device("cuda", 0)
     bf = torch.bfloat16
@@ -37,6 +40,21 @@ def make(mode: str, rows: int | None):
         x = torch.randn(rows or 24800, 4096, device=dev, dtype=bf)
         w = torch.randn(4096, 4096, device=dev, dtype=bf) * 0.02
         return lambda: linear(x, w)
+    if mode == "qo_cublas":  # the same shape on cuBLAS, for side-by-side counters
+        x = torch.randn(rows or 24800, 4096, device=dev, dtype=bf)
+        w = torch.randn(4096, 4096, device=dev, dtype=bf) * 0.02
+        return lambda: torch.nn.functional.linear(x, w)
+    if mode == "qk_prep":
+        b, s, hq, hk, d = (rows or 8), 3100, 32, 8, 128
+        q = torch.randn(b, s, hq * d, device=dev, dtype=bf).view(b, s, hq, d)
+        k = torch.randn(b, s, hk * d, device=dev, dtype=bf).view(b, s, hk, d)
+        v = torch.randn_like(k)
+        qw = torch.ones(d, device=dev, dtype=bf)
+        c = torch.randn(b, s, d, device=dev, dtype=bf)
+        sn = torch.randn_like(c)
+        kb = torch.zeros(b, hk, s + 72, d, device=dev, dtype=bf)
+        vb = torch.zeros_like(kb)
+        return lambda: qk_norm_rope_kv(q, k, v, qw, qw, 1e-6, 1e-6, c, sn, kb, vb, 0)
     if mode == "add_rmsnorm":
         x = torch.randn(3100, 4096, device=dev, dtype=bf)
         r = torch.randn_like(x)
