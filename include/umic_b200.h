@@ -20,6 +20,7 @@
 #ifndef UMIC_B200_H_
 #define UMIC_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -47,6 +48,9 @@ extern "C" {
 /* dtype codes for optional fp32 side inputs */
 #define UMIC_DTYPE_BF16 0
 #define UMIC_DTYPE_FP32 1
+
+/* GEMV flags */
+#define UMIC_GEMV_WEIGHTS_READY 1u /* weights not written by the preceding stream op */
 
 /* GEMM epilogues */
 #define UMIC_EPI_NONE 0
@@ -168,26 +172,49 @@ UMIC_API int umic_qk_norm_rope_kv(
 /* Row-count regime below FUSE_MIN_ROWS (integrate.py:27-30): HBM-bound GEMV,
  * y[m, n] = sum_k x[m, k] * w[n, k] (+ bias[n]); m < 64. w is [n, k] row-major
  * (nn.Linear layout). Replaces the cuBLAS fallback of _patched_linear_forward
- * (integrate.py:104-105). bias may be NULL. */
+ * (integrate.py:104-105). bias may be NULL.
+ *
+ * workspace: scratch of at least umic_gemv_workspace_bytes(n) bytes, 256-byte
+ * aligned, zero-filled before its first use; every call leaves it zeroed again.
+ * With a workspace, m <= 16 runs the streaming engine (TMA-fed, one CTA per SM,
+ * deterministic fixed-order reduction, programmatic dependent launch); with
+ * workspace == NULL (or m > 16) the cluster split-K engine runs, which needs no
+ * scratch. Calls sharing one workspace must be ordered on one stream: overlapping
+ * calls race on it. The same applies to the two calls below.
+ *
+ * flags: 0 or UMIC_GEMV_WEIGHTS_READY. The streaming engine is launched with
+ * programmatic stream serialization, so it may start while the previous kernel in
+ * the stream is finishing; x, y, bias and the workspace are only touched after that
+ * kernel completes. With UMIC_GEMV_WEIGHTS_READY the caller promises that the
+ * weights are not written by the operation enqueued just before this call, and the
+ * weight stream begins at once (e.g. model parameters inside a forward pass). */
 UMIC_API int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
-              void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* stream);
+                       void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace,
+                       size_t workspace_bytes, uint32_t flags, void* stream);
+
+/* Bytes of workspace the streaming engine needs for `rows` weight rows in one call
+ * (for umic_gemv_multi: the sum of n_i) on the current device. */
+UMIC_API size_t umic_gemv_workspace_bytes(int64_t rows);
 
 /* Up to 3 GEMVs sharing x in one launch (e.g. the q, k and v projections of a
  * decode step): y_i = x . w_i^T (+ bias_i) for i < count, with w_i [n_i, k],
  * y_i [m, n_i] (leading dimension ldy_i). Every n_i but the last must be a
- * multiple of 16. Host arrays of length count; bias may be NULL (or hold NULLs).
+ * multiple of 16 (of 64 for the streaming engine; otherwise the cluster engine
+ * runs). Host arrays of length count; bias may be NULL (or hold NULLs).
  * No reference counterpart as one call: replaces the q_proj / k_proj / v_proj
  * calls of one decode step (integrate.py:98-107 and the cuBLAS k/v sites). */
 UMIC_API int umic_gemv_multi(const void* x, int64_t ldx, int32_t count, const void* const* w,
                              const int64_t* ldw, const int64_t* n, const void* const* bias,
                              void* const* y, const int64_t* ldy, int64_t m, int64_t k,
+                             void* workspace, size_t workspace_bytes, uint32_t flags,
                              void* stream);
 
 /* h[m, n] = silu(x . wg[n]) * (x . wu[n]) for m < 64 rows.
  * Replaces the small-row branch of _fused_mlp_forward (integrate.py:48-50). */
 UMIC_API int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg, const void* wu,
-                            int64_t ldw, void* h, int64_t ldh, int64_t m, int64_t n,
-                            int64_t k, void* stream);
+                                     int64_t ldw, void* h, int64_t ldh, int64_t m, int64_t n,
+                                     int64_t k, void* workspace, size_t workspace_bytes,
+                                     uint32_t flags, void* stream);
 
 /* Tensor-core (tcgen05 + TMEM, TMA-fed) GEMM: y = epi(x . w^T + bias) + residual.
  * x [m, k], w [n, k] (both K-major), y [m, n]. bias / residual may be NULL.

@@ -14,7 +14,7 @@ HEADER = ROOT / "include" / "umic_b200.h"
 
 
 def _declared() -> list[str]:
-    return re.findall(r"UMIC_API\s+(?:int|const char\*)\s+(umic_\w+)\(", HEADER.read_text())
+    return re.findall(r"UMIC_API\s+(?:int|size_t|const char\*)\s+(umic_\w+)\(", HEADER.read_text())
 
 
 def test_library_exports_every_declared_symbol():
@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert _lib.lib().umic_abi_version() == 1
+    assert _lib.lib().umic_abi_version() == 2
 
 
 def test_null_pointer_rejected_on_host():
@@ -43,12 +43,22 @@ def test_bad_sizes_rejected_on_host():
     assert L.umic_gemm(fake, 8, fake, 8, None, None, 0, fake, 8, 4, 4, 0, 0, None) == 1
     assert L.umic_gemm(fake, 12, fake, 12, None, None, 0, fake, 16, 4, 16, 12, 0, None) == 3
     assert "multiple of 8" in _lib.last_message()
-    assert L.umic_gemv(fake, 8, fake, 8, None, fake, 8, 65, 8, 8, None) == 2
+    assert L.umic_gemv(fake, 8, fake, 8, None, fake, 8, 65, 8, 8, None, 0, 0, None) == 2
     assert L.umic_rope_inplace(fake, 0, 0, 0, 1, None, 0, 0, 0, 0, fake, fake, 0, 0, 0, 1, 1, 7,
                                None) == 1
     assert L.umic_kv_append(fake, fake, 0, 0, 0, 10, fake, 0, 0, 0, fake, 0, 0, 0, 1, 1, 4, 8,
                             8, None, None) == 5
     assert "overflow" in _lib.last_message()
+
+
+def test_gemv_workspace_contract_on_host():
+    """The workspace size grows with the rows of a call; a workspace that is too small
+    or misaligned is rejected before any launch (only checked once the streaming
+    engine is chosen, which needs the SM count of a device)."""
+    L = _lib.lib()
+    fake = ctypes.c_void_p(16)
+    # m > 64 is rejected whatever the workspace
+    assert L.umic_gemv(fake, 8, fake, 8, None, fake, 8, 65, 8, 8, fake, 1 << 20, 0, None) == 2
 
 
 def test_empty_work_is_a_noop():

@@ -273,6 +273,88 @@ def test_gemv_gate_silu_mul(cuda, m, n, k):
     _close(h, oracle.gate_silu_mul(x.cpu(), wg.cpu().t(), wu.cpu().t()))
 
 
+# ------------------------------------------- GEMV engines (streaming vs cluster)
+
+def _gemv_abi(x, w, bias, ws, flags=0):
+    """umic_gemv through the C ABI with an explicit workspace (ptr, bytes) or none."""
+    m, k = x.shape
+    n = w.shape[0]
+    y = torch.empty(m, n, device=x.device, dtype=torch.bfloat16)
+    _lib.call("umic_gemv", x.device, x.data_ptr(), k, w.data_ptr(), k, _lib.ptr(bias),
+              y.data_ptr(), n, m, n, k, ws[0], ws[1], flags)
+    return y
+
+
+@pytest.mark.parametrize("m,n,k", [(8, 4096, 4096), (1, 1000, 4104), (16, 64, 37888),
+                                   (9, 3000, 520), (2, 151936, 256)])
+def test_gemv_streaming_engine(cuda, m, n, k):
+    """With a workspace (streaming engine) and without (cluster engine) the result matches
+    the oracle; two streaming calls in a row are bit-identical (the kernel returns the
+    workspace counters to zero and reduces split row blocks in a fixed order)."""
+    x = _randn(m, k, seed=240, dev=cuda)
+    w = _randn(n, k, seed=241, dev=cuda, scale=0.02)
+    bias = _randn(n, seed=242, dev=cuda)
+    ws = _lib.gemv_workspace(cuda, n)
+    assert ws[0] is not None and ws[1] >= _lib.lib().umic_gemv_workspace_bytes(n)
+    y1 = _gemv_abi(x, w, bias, ws)
+    y2 = _gemv_abi(x, w, bias, ws)
+    torch.cuda.synchronize()  # the weights are settled: they may be streamed early
+    y3 = _gemv_abi(x, w, bias, ws, flags=_lib.GEMV_WEIGHTS_READY)
+    y0 = _gemv_abi(x, w, bias, (None, 0))
+    assert torch.equal(y1, y2) and torch.equal(y1, y3)
+    ref = oracle.linear(x.cpu(), w.cpu(), bias.cpu())
+    _close(y1, ref)
+    _close(y0, ref)
+    assert _lib.device_errors(cuda, clear=True) == 0
+
+
+def test_gemv_streaming_workspace_reuse_across_shapes(cuda):
+    """One workspace serves calls of growing and shrinking row counts in any order (the
+    counters of a larger call must find zeros, whatever earlier calls left in the slots)."""
+    ws = _lib.gemv_workspace(cuda, 40000)
+    for i, (m, n, k) in enumerate([(1, 256, 4096), (8, 4096, 4096), (2, 12288, 2048),
+                                   (1, 40000, 512), (8, 1000, 4096), (4, 12288, 4096)]):
+        x = _randn(m, k, seed=260 + i, dev=cuda)
+        w = _randn(n, k, seed=270 + i, dev=cuda, scale=0.02)
+        _close(_gemv_abi(x, w, None, ws), oracle.linear(x.cpu(), w.cpu()))
+
+
+def test_gemv_streaming_workspace_checks(cuda):
+    x = _randn(8, 512, seed=243, dev=cuda)
+    w = _randn(256, 512, seed=244, dev=cuda, scale=0.02)
+    ptr, size = _lib.gemv_workspace(cuda, 256)
+    with pytest.raises(_lib.UmicError, match="workspace"):
+        _gemv_abi(x, w, None, (ptr, 1024))
+    with pytest.raises(_lib.UmicError, match="aligned"):
+        _gemv_abi(x, w, None, (ptr + 16, size - 16))
+    with pytest.raises(_lib.UmicError, match="flags"):
+        _gemv_abi(x, w, None, (ptr, size), flags=6)
+    # the workspace is untouched by rejected calls: a proper call still matches
+    _close(_gemv_abi(x, w, None, (ptr, size)), oracle.linear(x.cpu(), w.cpu()))
+
+
+def test_gemv_multi_unaligned_segments_use_cluster_engine(cuda):
+    """Segment boundaries off the 64-row grid of the streaming engine run the cluster
+    engine (boundaries on 16 rows), with the same results."""
+    x = _randn(4, 1024, seed=245, dev=cuda)
+    ws = [_randn(n, 1024, seed=246 + i, dev=cuda, scale=0.02) for i, n in enumerate((1008, 40))]
+    stats.clear()
+    outs = linear_gemv_multi(x, ws)
+    assert stats["umic_gemv_multi"] == 1
+    for o, w in zip(outs, ws):
+        _close(o, oracle.linear(x.cpu(), w.cpu()))
+
+
+def test_gemv_gated_streaming_repeatable(cuda):
+    x = _randn(8, 4096, seed=250, dev=cuda)
+    wg = _randn(12288, 4096, seed=251, dev=cuda, scale=0.02)
+    wu = _randn(12288, 4096, seed=252, dev=cuda, scale=0.02)
+    h1 = gate_silu_mul_nk(x, wg, wu)
+    h2 = gate_silu_mul_nk(x, wg, wu)
+    assert torch.equal(h1, h2)
+    _close(h1, oracle.gate_silu_mul(x.cpu(), wg.cpu().t(), wu.cpu().t()))
+
+
 # ------------------------------------------------------------------ GEMM
 
 def _gpu_ref_linear(x, w, bias=None, act=None, residual=None):

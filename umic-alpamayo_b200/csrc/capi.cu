@@ -69,7 +69,7 @@ int sm_count() {
 
 extern "C" {
 
-int umic_abi_version(void) { return 1; }
+int umic_abi_version(void) { return 2; }
 
 const char* umic_last_error_message(void) { return umic::g_msg; }
 

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <cstdarg>
+#include <mutex>
 #include <cstdio>
 
 #include "../../include/umic_b200.h"
@@ -30,6 +31,22 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Asks (once per device) for the largest shared-memory carveout for `Kernel`. The
+// small streaming kernels that precede a streaming GEMV then leave their SMs
+// configured so the GEMV's CTAs (about 193 KB of shared memory) can become
+// resident beside them as soon as they allow the dependent launch.
+template <auto Kernel>
+inline void prefer_max_shared() {
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [] {
+    cudaFuncSetAttribute(Kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    cudaGetLastError();  // a refusal only costs the overlap
+  });
+}
+
 // Maps the launch status to UMIC_ERR_LAUNCH with the CUDA error string.
 inline int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
@@ -38,6 +55,14 @@ inline int launch_status(const char* what) {
 }
 
 // -------------------------------------------------------------- device side
+
+// Lets the next kernel in the stream begin launching now if it was launched with
+// programmatic stream serialization (the streaming GEMV is). That kernel still
+// waits for this grid to complete (griddepcontrol.wait) before it reads anything
+// this grid writes; without such a dependent this is a no-op.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Eight bf16 values travel as one 16-byte vector.
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {

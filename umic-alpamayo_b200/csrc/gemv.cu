@@ -22,7 +22,10 @@
 // silu(g) * u before the single bf16 rounding (fused_ffn.py:86-87 semantics).
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace umic {
 namespace {
@@ -70,6 +73,7 @@ namespace cg = cooperative_groups;
 
 template <int MC, bool kGated>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
+  allow_dependent_launch();
   // Weight slabs loaded before any math: 8 for the plain small-M case (2 KB of
   // loads in flight per lane-group of the warp), 4 when registers are scarcer.
   constexpr int kUnroll = (!kGated && MC <= 2) ? 8 : 4;
@@ -255,6 +259,437 @@ int check(const char* name, const void* x, int64_t ldx, const void* w, const voi
   return UMIC_OK;
 }
 
+// =================================================================== streaming
+//
+// Decode rows (m <= 16) with a caller-owned workspace take this engine. The weight
+// stream, which is all that matters at HBM speed, is moved by TMA instead of by the
+// math warps:
+//   - one persistent CTA per SM; the weight rows are cut into 64-row blocks and each
+//     block into k chunks (256 columns, 128 for gate+up), a "unit" of 32 KB;
+//   - the units are dealt to the CTAs as contiguous, equal ranges (stream-K), so
+//     every SM streams the same number of bytes whatever the matrix shape;
+//   - a producer warp keeps a 6-stage ring of units in flight (2D TMA loads with
+//     128-byte swizzle, 192 KB per SM); four consumer warps read their 16 rows of
+//     each unit from shared memory as the same permuted-k mma.sync fragments as the
+//     cluster engine above, with x (tiny, L1/L2 resident) from global memory;
+//   - a row block split between CTAs meets in the workspace: each contributor
+//     stores its fp32 partial in its own slot and counts itself in with an
+//     acq_rel atomic; the last one sums the slots in CTA order (deterministic),
+//     writes y and resets the counter to zero for the next call;
+//   - launched with programmatic stream serialization: CTA launch and barrier
+//     setup overlap the end of the previous kernel in the stream; the consumers
+//     wait for that kernel (griddepcontrol.wait) before touching x, y or the
+//     workspace. With UMIC_GEMV_WEIGHTS_READY the producer starts streaming the
+//     weights before the wait, i.e. while the previous kernel is still running;
+//     without it the producer waits too.
+constexpr int kStRows = 64;
+constexpr int kStStages = 6;
+constexpr uint32_t kStStageBytes = 32768;
+constexpr int kStConsumers = 4;
+constexpr int kStThreads = (kStConsumers + 1) * 32;
+constexpr int kStMaxContrib = 8;
+constexpr size_t kStSmem = kStStages * kStStageBytes + 1024 + 256;
+constexpr int kStPlane = kStRows * 16;  // one [64 rows][16 x rows] fp32 partial
+constexpr size_t kStCtaSlotBytes = 2 /*first, last block*/ * 2 /*gate, up*/ * kStPlane * 4;
+
+struct StreamArgs {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  __nv_bfloat16* y[kMaxSeg];
+  int64_t ldy[kMaxSeg];
+  const __nv_bfloat16* bias[kMaxSeg];
+  int row0[kMaxSeg + 1];  // segment starts in the concatenated row space (multiples of 64)
+  int nseg;
+  int m, k;
+  int nkc;    // k chunks per row block
+  int units;  // row blocks * nkc
+  int ctas;
+  float* slots;   // [ctas][first, last][gate, up][64][16]
+  unsigned* cnt;  // [row blocks], zero between calls (after the slots)
+  uint32_t* err;
+  int weights_ready;  // the weights may be read before the previous kernel completes
+};
+
+__device__ __forceinline__ int st_unit_begin(int c, const StreamArgs& a) {
+  return static_cast<int>((static_cast<long long>(c) * a.units) / a.ctas);
+}
+// CTA whose range holds unit u.
+__device__ __forceinline__ int st_cta_of(int u, const StreamArgs& a) {
+  return static_cast<int>(((static_cast<long long>(u) + 1) * a.ctas + a.units - 1) / a.units) - 1;
+}
+// Byte address of 16-byte chunk `chunk` of row r in a 128-byte-swizzled [64 x 64] box.
+__device__ __forceinline__ uint32_t st_swz(uint32_t box, int r, int chunk) {
+  return box + r * 128 + ((chunk ^ (r & 7)) << 4);
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ int st_segment(int row, const StreamArgs& a) {
+  int si = 0;
+  while (si + 1 < a.nseg && row >= a.row0[si + 1]) ++si;
+  return si;
+}
+
+template <int MC, bool kGated>
+__global__ void __launch_bounds__(kStThreads, 1)
+    gemv_stream_kernel(const __grid_constant__ CUtensorMap m0,
+                       const __grid_constant__ CUtensorMap m1,
+                       const __grid_constant__ CUtensorMap m2, StreamArgs a) {
+  constexpr int kKC = kGated ? 128 : 256;  // k columns per unit
+  constexpr int kSlabs = kKC / 32;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStStages * kStStageBytes);
+  // flags[0]: abort, flags[1]: "this CTA finishes the current row block"
+  volatile int* flags = reinterpret_cast<volatile int*>(bars + 2 * kStStages);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStStages);
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  const int u0 = st_unit_begin(c, a), u1 = st_unit_begin(c + 1, a);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kStConsumers);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&m0);
+    if (kGated || a.nseg > 1) prefetch_map(&m1);
+    if (a.nseg > 2) prefetch_map(&m2);
+  }
+  __syncthreads();
+  // The next kernel in the stream may begin its own prologue now.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == kStConsumers) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      if (!a.weights_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued = false, ok = true;
+      for (int u = u0; u < u1; ++u) {
+        const int rb = u / a.nkc, kc = u - rb * a.nkc;
+        const int si = st_segment(rb * kStRows, a);
+        const CUtensorMap* map = si == 0 ? &m0 : (si == 1 ? &m1 : &m2);
+        const int rin = rb * kStRows - a.row0[si];
+        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, a.err, flags)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = full0 + 8 * stage;
+        const uint32_t dst = sbase + stage * kStStageBytes;
+        mbar_expect_tx(fb, kStStageBytes);  // out-of-range rows / columns arrive as zeros
+        if constexpr (kGated) {
+          tma_load_2d(dst, &m0, fb, kc * kKC, rin);
+          tma_load_2d(dst + 8192, &m0, fb, kc * kKC + 64, rin);
+          tma_load_2d(dst + 16384, &m1, fb, kc * kKC, rin);
+          tma_load_2d(dst + 24576, &m1, fb, kc * kKC + 64, rin);
+        } else {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) tma_load_2d(dst + b * 8192, map, fb, kc * kKC + b * 64, rin);
+        }
+        issued = true;
+        if (++stage == kStStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok) {
+        // Every stage released by the consumers before the CTA may exit.
+        for (int s = 0; s < kStStages; ++s) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, a.err, flags)) break;
+          if (++stage == kStStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      } else if (issued) {
+        // Aborting: give copies in flight time to land before shared memory goes away.
+        const long long t0 = clock64();
+        while (clock64() - t0 < 4000000LL) {
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int g = lane >> 2, t = lane & 3;
+  const int r0 = warp * 16 + g, r1 = r0 + 8;  // rows inside the 64-row block
+  float acc[MC][4], acc2[kGated ? MC : 1][4];
+  auto zero_acc = [&]() {
+#pragma unroll
+    for (int i = 0; i < MC; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[i][j] = 0.f;
+        if constexpr (kGated) acc2[i][j] = 0.f;
+      }
+  };
+  zero_acc();
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  // x, y and the workspace may still belong to the previous kernel in the stream.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // Writes row block rb: directly when this CTA holds all of it, else via the slots.
+  auto flush = [&](int rb) {
+    const int first = st_cta_of(rb * a.nkc, a), last = st_cta_of((rb + 1) * a.nkc - 1, a);
+    const int contrib = last - first + 1;
+    const int si = st_segment(rb * kStRows, a);
+    const int rows_in_seg = a.row0[si + 1] - a.row0[si];
+    const int rin = rb * kStRows - a.row0[si];
+    auto emit = [&](int rr, int mcol, float v, float v2) {
+      const int nrow = rin + rr;
+      if (nrow >= rows_in_seg || mcol >= a.m) return;
+      float o;
+      if constexpr (kGated) {
+        o = v / (1.f + __expf(-v)) * v2;
+      } else {
+        o = v;
+        if (a.bias[si]) o += bf(a.bias[si][nrow]);
+      }
+      a.y[si][mcol * a.ldy[si] + nrow] = __float2bfloat16_rn(o);
+    };
+    if (contrib == 1) {
+#pragma unroll
+      for (int mc = 0; mc < MC; ++mc)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          emit(j < 2 ? r0 : r1, mc * 8 + 2 * t + (j & 1), acc[mc][j], kGated ? acc2[mc][j] : 0.f);
+      return;
+    }
+    // slot 0 holds a CTA's first row block, slot 1 its last one
+    auto slot_of = [&](int cta) {
+      const int side = (rb == st_unit_begin(cta, a) / a.nkc) ? 0 : 1;
+      return a.slots + (static_cast<size_t>(cta) * 2 + side) * 2 * kStPlane;
+    };
+    float* mine = slot_of(c);
+#pragma unroll
+    for (int mc = 0; mc < MC; ++mc)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int rr = j < 2 ? r0 : r1, mcol = mc * 8 + 2 * t + (j & 1);
+        __stcg(mine + rr * 16 + mcol, acc[mc][j]);
+        if constexpr (kGated) __stcg(mine + kStPlane + rr * 16 + mcol, acc2[mc][j]);
+      }
+    asm volatile("bar.sync 1, %0;" ::"n"(kStConsumers * 32) : "memory");
+    if (warp == 0 && lane == 0) {
+      // release: the partial stored above (ordered by the barrier) is visible with the
+      // count; acquire: the last arrival sees every other contributor's partial
+      unsigned prev;
+      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                   : "=r"(prev)
+                   : "l"(a.cnt + rb)
+                   : "memory");
+      flags[1] = prev == static_cast<unsigned>(contrib - 1);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kStConsumers * 32) : "memory");
+    if (!flags[1]) return;
+    // All partial loads in flight at once, then sums in CTA order.
+    constexpr int kVals = MC * 4 * (kGated ? 2 : 1);
+    float part[kStMaxContrib][kVals];
+#pragma unroll
+    for (int q = 0; q < kStMaxContrib; ++q) {
+      if (q < contrib) {
+        const float* src = slot_of(first + q);
+#pragma unroll
+        for (int mc = 0; mc < MC; ++mc)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int rr = j < 2 ? r0 : r1, mcol = mc * 8 + 2 * t + (j & 1);
+            part[q][mc * 4 + j] = __ldcg(src + rr * 16 + mcol);
+            if constexpr (kGated) part[q][MC * 4 + mc * 4 + j] = __ldcg(src + kStPlane + rr * 16 + mcol);
+          }
+      }
+    }
+#pragma unroll
+    for (int mc = 0; mc < MC; ++mc)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v = 0.f, v2 = 0.f;
+#pragma unroll
+        for (int q = 0; q < kStMaxContrib; ++q) {
+          if (q < contrib) {
+            v += part[q][mc * 4 + j];
+            if constexpr (kGated) v2 += part[q][MC * 4 + mc * 4 + j];
+          }
+        }
+        emit(j < 2 ? r0 : r1, mc * 8 + 2 * t + (j & 1), v, v2);
+      }
+    asm volatile("bar.sync 1, %0;" ::"n"(kStConsumers * 32) : "memory");
+    if (warp == 0 && lane == 0) {
+      a.cnt[rb] = 0;  // ready for the next call
+      flags[1] = 0;
+    }
+  };
+
+  int stage = 0;
+  uint32_t phase = 0;
+  int cur = -1;
+  for (int u = u0; u < u1; ++u) {
+    const int rb = u / a.nkc, kc = u - rb * a.nkc;
+    if (rb != cur) {
+      if (cur >= 0) {
+        flush(cur);
+        zero_acc();
+      }
+      cur = rb;
+    }
+    // this chunk's activations, requested before the weights land
+    uint4 xv[kSlabs][MC];
+#pragma unroll
+    for (int s = 0; s < kSlabs; ++s) {
+      const int kk = kc * kKC + s * 32 + t * 8;
+#pragma unroll
+      for (int mc = 0; mc < MC; ++mc) {
+        const int xr = mc * 8 + g;
+        xv[s][mc] = (kk < a.k && xr < a.m) ? ld_cached(a.x + xr * a.ldx + kk) : zero;
+      }
+    }
+    // Every consumer warp passes or fails the same waits, so none is left alone at a
+    // named barrier when another gives up.
+    if (!mbar_wait(full0 + 8 * stage, phase, a.err, flags)) return;
+    const uint32_t st = sbase + stage * kStStageBytes;
+#pragma unroll
+    for (int s = 0; s < kSlabs; ++s) {
+      const uint32_t box = st + (s >> 1) * 8192;
+      const int chunk = (s & 1) * 4 + t;
+      const uint4 wl = lds128(st_swz(box, r0, chunk));
+      const uint4 wh = lds128(st_swz(box, r1, chunk));
+#pragma unroll
+      for (int mc = 0; mc < MC; ++mc) slab_mma(acc[mc], wl, wh, xv[s][mc]);
+      if constexpr (kGated) {
+        const uint4 ul = lds128(st_swz(box + 16384, r0, chunk));
+        const uint4 uh = lds128(st_swz(box + 16384, r1, chunk));
+#pragma unroll
+        for (int mc = 0; mc < MC; ++mc) slab_mma(acc2[mc], ul, uh, xv[s][mc]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * stage);
+    if (++stage == kStStages) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+  if (cur >= 0) flush(cur);
+}
+
+inline size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+// Workspace of the streaming engine: one pair of partial slots per CTA (one CTA
+// per SM), then the row-block counters. The counters sit at the same offset for
+// every call on a device, so a call with more row blocks than any before it finds
+// zeros there (slots are never written over counters).
+size_t stream_counter_offset() {
+  return align256(static_cast<size_t>(sm_count()) * kStCtaSlotBytes);
+}
+size_t stream_workspace_bytes(int64_t rows) {
+  const int64_t blocks = (rows + kStRows - 1) / kStRows;
+  return stream_counter_offset() + align256(static_cast<size_t>(blocks) * 4);
+}
+
+// The streaming engine covers m <= 16 and segment starts on 64-row boundaries.
+bool stream_eligible(const GemvArgs& a) {
+  if (a.m > 16) return false;
+  for (int i = 1; i < a.nseg; ++i)
+    if (a.seg[i].row0 % kStRows) return false;
+  return true;
+}
+
+template <int MC, bool kGated>
+int stream_launch(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes,
+                  uint32_t flags, cudaStream_t st) {
+  static std::once_flag attr_once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once[dev >= 0 && dev < 64 ? dev : 0], [&] {
+    attr_err = cudaFuncSetAttribute(gemv_stream_kernel<MC, kGated>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kStSmem));
+  });
+  if (attr_err != cudaSuccess)
+    return fail(UMIC_ERR_LAUNCH, "%s: smem attribute: %s", name, cudaGetErrorString(attr_err));
+  CUtensorMap maps[kMaxSeg];
+  for (int i = 0; i < kMaxSeg; ++i) {
+    const Seg& sg = a.seg[i < a.nseg ? i : 0];
+    const void* base = (kGated && i == 1) ? static_cast<const void*>(a.w2) : sg.w;
+    if (!make_map(&maps[i], base, sg.rows, a.k, sg.ldw, kStRows))
+      return fail(UMIC_ERR_DEVICE, "%s: cuTensorMapEncodeTiled unavailable or rejected", name);
+  }
+  StreamArgs s{};
+  s.x = a.x;
+  s.ldx = a.ldx;
+  for (int i = 0; i < a.nseg; ++i) {
+    s.y[i] = a.seg[i].y;
+    s.ldy[i] = a.seg[i].ldy;
+    s.bias[i] = a.seg[i].bias;
+    s.row0[i] = a.seg[i].row0;
+  }
+  s.row0[a.nseg] = a.n;
+  s.nseg = a.nseg;
+  s.m = a.m;
+  s.k = a.k;
+  constexpr int kKC = kGated ? 128 : 256;
+  s.nkc = (a.k + kKC - 1) / kKC;
+  const int64_t blocks = (static_cast<int64_t>(a.n) + kStRows - 1) / kStRows;
+  const int64_t units = blocks * s.nkc;
+  if (units > 0x7fffffffLL / 256)
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: matrix too large for the streaming engine", name);
+  s.units = static_cast<int>(units);
+  // At least ceil(nkc / 7) units per CTA keeps a row block within 8 contributors.
+  const int per = (s.nkc + kStMaxContrib - 2) / (kStMaxContrib - 1);
+  const int64_t by_units = units / per;
+  s.ctas = static_cast<int>(by_units < sm_count() ? (by_units > 0 ? by_units : 1) : sm_count());
+  const size_t need = stream_workspace_bytes(a.n);
+  if (ws_bytes < need)
+    return fail(UMIC_ERR_INVALID_ARG, "%s: workspace of %zu bytes, %zu needed", name, ws_bytes,
+                need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u)
+    return fail(UMIC_ERR_ALIGNMENT, "%s: workspace must be 256-byte aligned", name);
+  s.slots = static_cast<float*>(ws);
+  s.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + stream_counter_offset());
+  s.err = device_error_word();
+  s.weights_ready = (flags & UMIC_GEMV_WEIGHTS_READY) ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(s.ctas, 1, 1);
+  cfg.blockDim = dim3(kStThreads, 1, 1);
+  cfg.dynamicSmemBytes = kStSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_stream_kernel<MC, kGated>, maps[0], maps[1],
+                                     maps[2], s);
+  if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", name, cudaGetErrorString(e));
+  return launch_status(name);
+}
+
+// Engine choice: streaming with a workspace, cluster split-K without one (or for
+// shapes the streaming engine does not cover).
+template <bool kGated>
+int run(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes, uint32_t flags,
+        cudaStream_t st) {
+  if (flags & ~static_cast<uint32_t>(UMIC_GEMV_WEIGHTS_READY))
+    return fail(UMIC_ERR_INVALID_ARG, "%s: unknown flags 0x%x", name, flags);
+  if (ws && stream_eligible(a))
+    return a.m <= 8 ? stream_launch<1, kGated>(name, a, ws, ws_bytes, flags, st)
+                    : stream_launch<2, kGated>(name, a, ws, ws_bytes, flags, st);
+  return dispatch<kGated>(a, st);
+}
+
 }  // namespace
 }  // namespace umic
 
@@ -263,7 +698,8 @@ using namespace umic;
 extern "C" {
 
 int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias, void* y,
-              int64_t ldy, int64_t m, int64_t n, int64_t k, void* stream) {
+              int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace,
+              size_t workspace_bytes, uint32_t flags, void* stream) {
   clear_error();
   if (int rc = check("umic_gemv", x, ldx, w, w, ldw, y, ldy, m, n, k)) return rc;
   if (m == 0 || n == 0) return UMIC_OK;  // nothing to launch
@@ -277,12 +713,13 @@ int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, const void
   a.n = static_cast<int>(n);
   a.k = static_cast<int>(k);
   a.slabs = static_cast<int>((k + 31) / 32);
-  return dispatch<false>(a, as_stream(stream));
+  return run<false>("umic_gemv", a, workspace, workspace_bytes, flags, as_stream(stream));
 }
 
 int umic_gemv_multi(const void* x, int64_t ldx, int32_t count, const void* const* w,
                     const int64_t* ldw, const int64_t* n, const void* const* bias,
-                    void* const* y, const int64_t* ldy, int64_t m, int64_t k, void* stream) {
+                    void* const* y, const int64_t* ldy, int64_t m, int64_t k, void* workspace,
+                    size_t workspace_bytes, uint32_t flags, void* stream) {
   clear_error();
   if (count < 1 || count > kMaxSeg || !w || !ldw || !n || !y || !ldy)
     return fail(UMIC_ERR_INVALID_ARG, "umic_gemv_multi: count=%d or null array", count);
@@ -310,11 +747,13 @@ int umic_gemv_multi(const void* x, int64_t ldx, int32_t count, const void* const
   a.n = static_cast<int>(total);
   a.k = static_cast<int>(k);
   a.slabs = static_cast<int>((k + 31) / 32);
-  return dispatch<false>(a, as_stream(stream));
+  return run<false>("umic_gemv_multi", a, workspace, workspace_bytes, flags,
+                    as_stream(stream));
 }
 
 int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg, const void* wu,
                             int64_t ldw, void* h, int64_t ldh, int64_t m, int64_t n, int64_t k,
+                            void* workspace, size_t workspace_bytes, uint32_t flags,
                             void* stream) {
   clear_error();
   if (int rc = check("umic_gemv_gate_silu_mul", x, ldx, wg, wu, ldw, h, ldh, m, n, k)) return rc;
@@ -330,7 +769,14 @@ int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg, const vo
   a.n = static_cast<int>(n);
   a.k = static_cast<int>(k);
   a.slabs = static_cast<int>((k + 31) / 32);
-  return dispatch<true>(a, as_stream(stream));
+  return run<true>("umic_gemv_gate_silu_mul", a, workspace, workspace_bytes, flags,
+                   as_stream(stream));
+}
+
+size_t umic_gemv_workspace_bytes(int64_t rows) {
+  clear_error();
+  if (rows < 0) return 0;
+  return stream_workspace_bytes(rows);
 }
 
 }  // extern "C"

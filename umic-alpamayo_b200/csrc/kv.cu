@@ -45,6 +45,7 @@ __device__ __forceinline__ bool resolve_pos(const KvArgs& a, int64_t& pos) {
 // grid = (token tiles, heads, batch); block = (chunks, tokens per block).
 template <bool kVec>
 __global__ void __launch_bounds__(256) kv_append_kernel(KvArgs a) {
+  allow_dependent_launch();
   int64_t pos;
   if (!resolve_pos(a, pos)) return;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;

@@ -56,6 +56,7 @@ __device__ __forceinline__ float group_sum(float v, float* red) {
 
 template <int TPR, int VPT, bool kAdd, bool kLayerNorm>
 __global__ void __launch_bounds__(kThreads) norm_vec_kernel(NormArgs a) {
+  allow_dependent_launch();
   constexpr int kRowsPerCta = kThreads / TPR;
   __shared__ float red[kThreads / 32];
   const int sub = threadIdx.x % TPR;
@@ -137,6 +138,7 @@ constexpr int kScalarMaxN = 16384;
 
 template <bool kAdd, bool kLayerNorm>
 __global__ void __launch_bounds__(kThreads) norm_scalar_kernel(NormArgs a) {
+  allow_dependent_launch();
   extern __shared__ float srow[];
   __shared__ float red[kThreads / 32];
   const int64_t row = blockIdx.x;
@@ -177,6 +179,7 @@ template <int TPR, int VPT, bool kAdd, bool kLN>
 void launch_vec(const NormArgs& a, cudaStream_t st) {
   constexpr int kRowsPerCta = kThreads / TPR;
   const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
+  prefer_max_shared<norm_vec_kernel<TPR, VPT, kAdd, kLN>>();
   norm_vec_kernel<TPR, VPT, kAdd, kLN><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(a);
 }
 
@@ -205,6 +208,7 @@ int dispatch(const NormArgs& a, bool vec_ok, cudaStream_t st) {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(norm_scalar_kernel<kAdd, kLN>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    prefer_max_shared<norm_scalar_kernel<kAdd, kLN>>();
     norm_scalar_kernel<kAdd, kLN><<<static_cast<unsigned>(a.rows), kThreads, smem, st>>>(a);
   }
   return launch_status("norm launch");

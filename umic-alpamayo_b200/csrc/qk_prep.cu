@@ -64,6 +64,7 @@ constexpr int kPrepThreads = 128;
 // which is what bounds this kernel (the work per byte is a few dozen instructions).
 template <int TPH, bool kCosFp32>
 __global__ void __launch_bounds__(kPrepThreads) qk_prep_kernel(PrepArgs a) {
+  allow_dependent_launch();
   constexpr int kRowsPerBlock = kPrepThreads / TPH;
   constexpr int kHalfD = TPH * 8;  // D / 2
   const int sub = threadIdx.x % TPH;
@@ -152,8 +153,13 @@ void launch_prep(const PrepArgs& a, int64_t seq, int64_t batch, int zblocks, boo
                  cudaStream_t st) {
   const dim3 grid(static_cast<unsigned>(seq), static_cast<unsigned>(batch),
                   static_cast<unsigned>(zblocks));
-  if (cos32) qk_prep_kernel<TPH, true><<<grid, kPrepThreads, 0, st>>>(a);
-  else qk_prep_kernel<TPH, false><<<grid, kPrepThreads, 0, st>>>(a);
+  if (cos32) {
+    prefer_max_shared<qk_prep_kernel<TPH, true>>();
+    qk_prep_kernel<TPH, true><<<grid, kPrepThreads, 0, st>>>(a);
+  } else {
+    prefer_max_shared<qk_prep_kernel<TPH, false>>();
+    qk_prep_kernel<TPH, false><<<grid, kPrepThreads, 0, st>>>(a);
+  }
 }
 
 }  // namespace

@@ -60,6 +60,7 @@ __device__ __forceinline__ __nv_bfloat16* locate(const RopeArgs& a, int64_t& cro
 
 template <bool kCosFp32>
 __global__ void __launch_bounds__(1024) rope_vec_kernel(RopeArgs a) {
+  allow_dependent_launch();
   int64_t crow;
   __nv_bfloat16* row = locate(a, crow);
   if (!row) return;
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(1024) rope_vec_kernel(RopeArgs a) {
 
 // Any even head_dim / alignment: one rotation pair per thread.
 __global__ void __launch_bounds__(1024) rope_scalar_kernel(RopeArgs a, bool cos_fp32) {
+  allow_dependent_launch();
   int64_t crow;
   __nv_bfloat16* row = locate(a, crow);
   if (!row) return;

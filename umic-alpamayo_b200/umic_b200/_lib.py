@@ -22,6 +22,8 @@ _c_i32 = ctypes.c_int32
 _c_int = ctypes.c_int
 _c_f32 = ctypes.c_float
 _c_p = ctypes.c_void_p
+_c_size = ctypes.c_size_t
+_c_u32 = ctypes.c_uint32
 
 # name -> argument types (all return int status unless listed in _RESTYPES)
 _SIGNATURES: dict[str, list] = {
@@ -42,12 +44,14 @@ _SIGNATURES: dict[str, list] = {
     "umic_kv_append": [_c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64,
                        _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i32, _c_i64, _c_i32, _c_i64,
                        _c_p, _c_p],
-    "umic_gemv": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p],
+    "umic_gemv": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
+                  _c_size, _c_u32, _c_p],
     "umic_gemv_gate_silu_mul": [_c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64,
-                                _c_i64, _c_p],
+                                _c_i64, _c_p, _c_size, _c_u32, _c_p],
     "umic_gemv_multi": [_c_p, _c_i64, _c_i32, ctypes.POINTER(_c_p), ctypes.POINTER(_c_i64),
                         ctypes.POINTER(_c_i64), ctypes.POINTER(_c_p), ctypes.POINTER(_c_p),
-                        ctypes.POINTER(_c_i64), _c_i64, _c_i64, _c_p],
+                        ctypes.POINTER(_c_i64), _c_i64, _c_i64, _c_p, _c_size, _c_u32, _c_p],
+    "umic_gemv_workspace_bytes": [_c_i64],
     "umic_qk_norm_rope_kv": [_c_p, _c_i64, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i64, _c_i64,
                              _c_p, _c_i64, _c_i64, _c_i64, _c_i32, _c_p, _c_p, _c_int, _c_f32,
                              _c_f32, _c_p, _c_p, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_i64,
@@ -57,7 +61,7 @@ _SIGNATURES: dict[str, list] = {
     "umic_gemm_gate_silu_mul": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64,
                                 _c_i64, _c_i64, _c_p],
 }
-_RESTYPES = {"umic_last_error_message": ctypes.c_char_p}
+_RESTYPES = {"umic_last_error_message": ctypes.c_char_p, "umic_gemv_workspace_bytes": _c_size}
 
 ERR_NAMES = {1: "INVALID_ARG", 2: "UNSUPPORTED", 3: "ALIGNMENT", 4: "LAUNCH", 5: "OVERFLOW",
              6: "DEVICE"}
@@ -68,6 +72,7 @@ ERR_OVERFLOW = 5
 DTYPE_BF16 = 0
 DTYPE_FP32 = 1
 EPI_NONE, EPI_GELU_ERF, EPI_GELU_TANH = 0, 1, 2
+GEMV_WEIGHTS_READY = 1
 DEVERR_KV_OVERFLOW = 1
 DEVERR_WAIT_TIMEOUT = 2
 
@@ -155,3 +160,33 @@ def device_errors(device: torch.device | None = None, clear: bool = True) -> int
 
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+_MIN_WORKSPACE = 8 << 20
+_workspaces: dict[int, torch.Tensor] = {}
+_retired: list[torch.Tensor] = []
+
+
+def gemv_workspace(device: torch.device, rows: int) -> tuple[int | None, int]:
+    """(pointer, bytes) of the streaming GEMV's scratch on `device` for `rows` weight rows.
+
+    One zero-filled buffer per device, kept for the life of the process: captured CUDA
+    graphs hold its address, so a buffer outgrown by a larger call is retired, never
+    freed. The kernel returns its counters to zero after every call. Calls that share
+    the buffer must be ordered on one stream (overlapping calls would race on it).
+    No buffer is created while a CUDA graph is being captured; such a call gets
+    (None, 0) and runs the workspace-free engine."""
+    _ensure_device(device)
+    need = int(lib().umic_gemv_workspace_bytes(rows))
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _workspaces.get(idx)
+    if buf is None or buf.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            return None, 0
+        if buf is not None:
+            _retired.append(buf)
+        buf = torch.zeros(max(need, _MIN_WORKSPACE), dtype=torch.uint8, device=device)
+        torch.cuda.current_stream(device).synchronize()  # zeroed before any stream uses it
+        _workspaces[idx] = buf
+    return buf.data_ptr(), buf.numel()
+

@@ -73,7 +73,7 @@ def _is_p5_mlp(module: nn.Module) -> bool:
 def _project(lin: nn.Linear, x2d: torch.Tensor, residual: torch.Tensor | None = None):
     """A Linear on the B200 kernels: GEMV below FUSE_MIN_ROWS, tcgen05 GEMM above."""
     if x2d.shape[0] < FUSE_MIN_ROWS and residual is None:
-        return linear_gemv(x2d, lin.weight, lin.bias)
+        return linear_gemv(x2d, lin.weight, lin.bias, weights_ready=True)
     return linear(x2d, lin.weight, lin.bias, residual=residual)
 
 
@@ -87,7 +87,7 @@ def mlp_forward(mlp: nn.Module, x: torch.Tensor,
     """
     shape = x.shape
     x2d = x.reshape(-1, shape[-1])
-    h = gate_silu_mul_nk(x2d, mlp.gate_proj.weight, mlp.up_proj.weight)
+    h = gate_silu_mul_nk(x2d, mlp.gate_proj.weight, mlp.up_proj.weight, weights_ready=True)
     r2d = residual.reshape(-1, residual.shape[-1]) if residual is not None else None
     out = _project(mlp.down_proj, h, r2d)
     return out.reshape(*shape[:-1], out.shape[-1])
@@ -145,7 +145,7 @@ def _decode_gemv_forward(self: nn.Linear, x: torch.Tensor) -> torch.Tensor:
     x2d = x.reshape(-1, shape[-1])
     if x2d.shape[0] >= FUSE_MIN_ROWS or not x2d.is_cuda or x2d.dtype != torch.bfloat16:
         return nn.functional.linear(x, self.weight, self.bias)
-    out = linear_gemv(x2d, self.weight, self.bias)
+    out = linear_gemv(x2d, self.weight, self.bias, weights_ready=True)
     return out.reshape(*shape[:-1], out.shape[-1])
 
 
@@ -204,7 +204,7 @@ def _fused_attention_forward(self, hidden_states, position_embeddings=None, atte
     if x2d.shape[0] < FUSE_MIN_ROWS:
         q, k, v = linear_gemv_multi(
             x2d, [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight],
-            [self.q_proj.bias, self.k_proj.bias, self.v_proj.bias])
+            [self.q_proj.bias, self.k_proj.bias, self.v_proj.bias], weights_ready=True)
     else:
         q = linear(x2d, self.q_proj.weight, self.q_proj.bias)
         k = nn.functional.linear(x2d, self.k_proj.weight, self.k_proj.bias)

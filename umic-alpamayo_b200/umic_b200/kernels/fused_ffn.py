@@ -26,9 +26,12 @@ def _nk_from_kn(w: torch.Tensor) -> torch.Tensor:
     return wt if wt.stride(-1) == 1 else wt.contiguous()
 
 
-def gate_silu_mul_nk(x2d: torch.Tensor, w_gate: torch.Tensor,
-                     w_up: torch.Tensor) -> torch.Tensor:
-    """h = silu(x2d @ w_gate.T) * (x2d @ w_up.T) with nn.Linear-layout weights [N, K]."""
+def gate_silu_mul_nk(x2d: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, *,
+                     weights_ready: bool = False) -> torch.Tensor:
+    """h = silu(x2d @ w_gate.T) * (x2d @ w_up.T) with nn.Linear-layout weights [N, K].
+
+    weights_ready (GEMV regime only): the weights are not written by the kernel
+    enqueued just before this call, so they may be streamed while it finishes."""
     dev = require_cuda("gate_silu_mul", x2d, w_gate, w_up)
     require_bf16("gate_silu_mul", x2d, w_gate, w_up)
     m, k = x2d.shape
@@ -47,9 +50,11 @@ def gate_silu_mul_nk(x2d: torch.Tensor, w_gate: torch.Tensor,
         if w_gate.stride(0) != w_up.stride(0):
             w_up = w_up.contiguous()
             w_gate = w_gate.contiguous()
+        ws, ws_bytes = _lib.gemv_workspace(dev, n)
         rc = _lib.try_call("umic_gemv_gate_silu_mul", dev, x2d.data_ptr(), row_stride(x2d),
                            w_gate.data_ptr(), w_up.data_ptr(), row_stride(w_gate),
-                           h.data_ptr(), n, m, n, k)
+                           h.data_ptr(), n, m, n, k, ws, ws_bytes,
+                           _lib.GEMV_WEIGHTS_READY if weights_ready else 0)
         name = "umic_gemv_gate_silu_mul"
     else:
         tok = probe_begin("umic_gemm_gate_silu_mul")

@@ -68,9 +68,13 @@ def linear(x2d: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = 
     return y
 
 
-def linear_gemv(x2d: torch.Tensor, weight: torch.Tensor,
-                bias: torch.Tensor | None = None) -> torch.Tensor:
-    """y = x2d @ weight.T + bias for x2d with fewer than 64 rows (weight-streaming)."""
+def linear_gemv(x2d: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
+                weights_ready: bool = False) -> torch.Tensor:
+    """y = x2d @ weight.T + bias for x2d with fewer than 64 rows (weight-streaming).
+
+    weights_ready: the weight is not written by the kernel enqueued just before this
+    call (true for module parameters inside a forward pass), so its stream may begin
+    while that kernel is finishing."""
     dev = require_cuda("linear_gemv", x2d, weight, bias)
     require_bf16("linear_gemv", x2d, weight, bias)
     m, k = x2d.shape
@@ -80,8 +84,10 @@ def linear_gemv(x2d: torch.Tensor, weight: torch.Tensor,
     x2d = _k_major(x2d)
     weight = _k_major(weight)
     y = torch.empty((m, n), device=x2d.device, dtype=x2d.dtype)
+    ws, ws_bytes = _lib.gemv_workspace(dev, n)
     rc = _lib.try_call("umic_gemv", dev, x2d.data_ptr(), row_stride(x2d), weight.data_ptr(),
-                       row_stride(weight), _lib.ptr(bias), y.data_ptr(), n, m, n, k)
+                       row_stride(weight), _lib.ptr(bias), y.data_ptr(), n, m, n, k, ws,
+                       ws_bytes, _lib.GEMV_WEIGHTS_READY if weights_ready else 0)
     if rc:
         stats["gemv_fallback"] += 1
         return F.linear(x2d, weight, bias)
@@ -90,7 +96,8 @@ def linear_gemv(x2d: torch.Tensor, weight: torch.Tensor,
 
 
 def linear_gemv_multi(x2d: torch.Tensor, weights: list[torch.Tensor],
-                      biases: list[torch.Tensor | None] | None = None) -> list[torch.Tensor]:
+                      biases: list[torch.Tensor | None] | None = None, *,
+                      weights_ready: bool = False) -> list[torch.Tensor]:
     """[x2d @ w.T + b for each w] in one launch (x2d with fewer than 64 rows); used for
     the q/k/v projections of a decode step."""
     import ctypes
@@ -107,10 +114,12 @@ def linear_gemv_multi(x2d: torch.Tensor, weights: list[torch.Tensor],
     outs = [torch.empty((m, w.shape[0]), device=x2d.device, dtype=x2d.dtype) for w in weights]
     P = ctypes.c_void_p * cnt
     I = ctypes.c_int64 * cnt
+    ws, ws_bytes = _lib.gemv_workspace(dev, sum(w.shape[0] for w in weights))
     rc = _lib.try_call("umic_gemv_multi", dev, x2d.data_ptr(), row_stride(x2d), cnt,
                        P(*[w.data_ptr() for w in weights]), I(*[row_stride(w) for w in weights]),
                        I(*[w.shape[0] for w in weights]), P(*[_lib.ptr(b) for b in biases]),
-                       P(*[o.data_ptr() for o in outs]), I(*[o.shape[1] for o in outs]), m, k)
+                       P(*[o.data_ptr() for o in outs]), I(*[o.shape[1] for o in outs]), m, k,
+                       ws, ws_bytes, _lib.GEMV_WEIGHTS_READY if weights_ready else 0)
     if rc:
         stats["gemv_fallback"] += 1
         return [F.linear(x2d, w, b) for w, b in zip(weights, biases)]
