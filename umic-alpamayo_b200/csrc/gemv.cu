@@ -608,7 +608,7 @@ bool stream_eligible(const GemvArgs& a) {
 
 template <int MC, bool kGated>
 int stream_launch(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes,
-                  uint32_t flags, cudaStream_t st) {
+                  uint32_t flags, cudaStream_t st, bool pdl = true) {
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -668,13 +668,48 @@ int stream_launch(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_stream_kernel<MC, kGated>, maps[0], maps[1],
                                      maps[2], s);
   if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", name, cudaGetErrorString(e));
   return launch_status(name);
+}
+
+// ------------------------------------------------------- allocation-free entry
+//
+// umic_gemv_noalloc runs the streaming engine on a scratch area that is part of
+// the library image: a file-scope __device__ array, created with the module on
+// each device, so the call itself allocates nothing. Its size bounds the calls it
+// takes (rows per call and SMs per device). One array per device serves every
+// such call on that device, from any stream or thread: overlapping calls race.
+constexpr int64_t kStaticMaxRows = int64_t{1} << 20;
+constexpr int kStaticMaxSms = 256;
+constexpr size_t kStaticScratchBytes =
+    kStaticMaxSms * kStCtaSlotBytes + static_cast<size_t>(kStaticMaxRows / kStRows) * 4;
+static __device__ __align__(256) unsigned char g_gemv_scratch[kStaticScratchBytes];
+
+// Device address of g_gemv_scratch on the current device, resolved once per device
+// (with that device current).
+int static_scratch(const char* name, void** out) {
+  static std::once_flag once[64];
+  static void* addr[64];
+  static cudaError_t status[64];
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(UMIC_ERR_DEVICE, "%s: cudaGetDevice: %s", name,
+                                    cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(UMIC_ERR_UNSUPPORTED, "%s: device %d", name, dev);
+  std::call_once(once[dev], [dev] {
+    status[dev] = cudaGetSymbolAddress(&addr[dev], g_gemv_scratch);
+    if (status[dev] != cudaSuccess) cudaGetLastError();
+  });
+  if (status[dev] != cudaSuccess)
+    return fail(UMIC_ERR_DEVICE, "%s: cudaGetSymbolAddress of the static scratch: %s", name,
+                cudaGetErrorString(status[dev]));
+  *out = addr[dev];
+  return UMIC_OK;
 }
 
 // Engine choice: streaming with a workspace, cluster split-K without one (or for
@@ -771,6 +806,48 @@ int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg, const vo
   a.slabs = static_cast<int>((k + 31) / 32);
   return run<true>("umic_gemv_gate_silu_mul", a, workspace, workspace_bytes, flags,
                    as_stream(stream));
+}
+
+int umic_gemv_noalloc(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+                      void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* stream) {
+  static const char* kName = "umic_gemv_noalloc";
+  clear_error();
+  if (int rc = check(kName, x, ldx, w, w, ldw, y, ldy, m, n, k)) return rc;
+  if (m == 0 || n == 0) return UMIC_OK;
+  if (m > 16)
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: m=%lld rows of x; the streaming engine takes 1..16",
+                kName, (long long)m);
+  if (n > kStaticMaxRows)
+    return fail(UMIC_ERR_UNSUPPORTED,
+                "%s: n=%lld weight rows exceed the static scratch maximum of %lld rows", kName,
+                (long long)n, (long long)kStaticMaxRows);
+  if (sm_count() > kStaticMaxSms)
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: %d SMs exceed the static scratch maximum of %d",
+                kName, sm_count(), kStaticMaxSms);
+  void* scratch = nullptr;
+  if (int rc = static_scratch(kName, &scratch)) return rc;
+  cudaStream_t st = as_stream(stream);
+  // The row-block counters must start at zero: clear this call's range on the stream
+  // (a kernel that ran out of its wait limit may have left some set).
+  const size_t counters = align256(static_cast<size_t>((n + kStRows - 1) / kStRows) * 4);
+  cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + stream_counter_offset(), 0,
+                                  counters, st);
+  if (e != cudaSuccess)
+    return fail(UMIC_ERR_LAUNCH, "%s: clearing the counters: %s", kName, cudaGetErrorString(e));
+  GemvArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.seg[0] = Seg{static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(bias),
+                 static_cast<__nv_bfloat16*>(y), ldw, ldy, 0, static_cast<int>(n)};
+  a.nseg = 1;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.slabs = static_cast<int>((k + 31) / 32);
+  // Plain stream order (no programmatic dependent launch): the memset above must
+  // complete before any CTA reads a counter.
+  return a.m <= 8 ? stream_launch<1, false>(kName, a, scratch, kStaticScratchBytes, 0, st, false)
+                  : stream_launch<2, false>(kName, a, scratch, kStaticScratchBytes, 0, st, false);
 }
 
 size_t umic_gemv_workspace_bytes(int64_t rows) {
