@@ -3,9 +3,12 @@
     python -m umic_b200.kernel_bench [--out results.json]
 
 Each case is timed with CUDA events around one launch after 3 warm-up launches,
-with a 256 MB buffer written between launches to flush L2; the median of 20 is
+with a 256 MB buffer read between launches to flush L2 (a read leaves no dirty
+lines whose write-back would land in the timed launch); the median of 20 is
 reported as (ms, GB/s or TFLOP/s). GEMM cases also report the relative error
-against cuBLAS on the same inputs.
+against cuBLAS on the same inputs. The decode GEMV shapes are also timed back to
+back over enough weight copies to exceed L2 (the regime of a decode step), for
+the streaming engine (with a workspace) and the cluster engine (without).
 """
 import json
 import sys
@@ -19,14 +22,14 @@ from umic_b200.kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inp
 def main() -> None:
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.int8, device=dev)
+    flush = torch.ones(64 * 1024 * 1024, dtype=torch.int32, device=dev)
 
     def t(fn, iters=20, flushl2=True):
         for _ in range(3): fn()
         torch.cuda.synchronize()
         ts = []
         for _ in range(iters):
-            if flushl2: flush.zero_()
+            if flushl2: flush.sum()
             s = torch.cuda.Event(enable_timing=True); e = torch.cuda.Event(enable_timing=True)
             s.record(); fn(); e.record(); torch.cuda.synchronize()
             ts.append(s.elapsed_time(e))
@@ -67,6 +70,33 @@ def main() -> None:
         W2 = torch.randn(151936, 4096, device=dev, dtype=bf)
         ms = t(lambda: linear_gemv(xs, W2)); res[f"gemv_m{m}_lmhead"] = (ms, W2.numel()*2/(ms*1e-3)/1e9)
         del W2
+    # decode GEMV engines, back to back over rotating weight copies (> 600 MB in total)
+    from umic_b200 import _lib
+
+    def gemv_call(xs, W, ws):
+        m_, k_ = xs.shape
+        n_ = W.shape[0]
+        y = torch.empty(m_, n_, device=dev, dtype=bf)
+        _lib.call("umic_gemv", dev, xs.data_ptr(), k_, W.data_ptr(), k_, None, y.data_ptr(), n_,
+                  m_, n_, k_, ws[0], ws[1], _lib.GEMV_WEIGHTS_READY if ws[0] else 0)
+
+    for (n, kd) in [(4096, 4096), (6144, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]:
+        copies = max(2, -(-600_000_000 // (n * kd * 2)))
+        Ws = [torch.randn(n, kd, device=dev, dtype=bf) for _ in range(copies)]
+        xs = torch.randn(8, kd, device=dev, dtype=bf)
+        for name, ws in (("stream", _lib.gemv_workspace(dev, n)), ("cluster", (None, 0))):
+            for i in range(3):
+                gemv_call(xs, Ws[i % copies], ws)
+            torch.cuda.synchronize()
+            reps = copies * 4
+            s0 = torch.cuda.Event(enable_timing=True); e0 = torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for i in range(reps):
+                gemv_call(xs, Ws[i % copies], ws)
+            e0.record(); torch.cuda.synchronize()
+            ms = s0.elapsed_time(e0) / reps
+            res[f"gemv_b2b_{name}_m8_{n}x{kd}"] = (ms, n * kd * 2 / (ms * 1e-3) / 1e9)
+        del Ws
     for kk_, v in res.items():
         print(kk_, v)
     if "--out" in sys.argv:
