@@ -247,9 +247,17 @@ def test_flow_expert_euler(cuda):
     stats.clear()
     x_ours = flow_sample(expert, _prefix_cache(18, E, 8, S, 128, cuda, torch.bfloat16), S,
                          x0.bfloat16())
-    integrate.unfuse_mlps(holder)
     assert stats["umic_gemm_gate_silu_mul"] == 18 * 10
     assert stats["umic_qk_norm_rope_kv"] == 18 * 10  # KV write fused into the attention prep
+    # the same 10 steps with one captured Euler step replayed: 2 eager warm-up steps, one
+    # side-stream pass before capture and the capture itself go through Python; the 8
+    # replays launch the same kernels from the graph
+    stats.clear()
+    x_graph = flow_sample(expert, _prefix_cache(18, E, 8, S, 128, cuda, torch.bfloat16), S,
+                          x0.bfloat16(), graph=True)
+    assert stats["umic_gemm_gate_silu_mul"] == 18 * 4
+    integrate.unfuse_mlps(holder)
+    assert oracle.rel_err(x_graph, x_ours) <= 1e-3, oracle.rel_err(x_graph, x_ours)
     e_ours, e_eager = oracle.max_rel_err(x_ours, x32), oracle.max_rel_err(x_eager, x32)
     l2_ours, l2_eager = oracle.rel_err(x_ours, x32), oracle.rel_err(x_eager, x32)
     print(f"flow 10 Euler steps vs fp32: max_rel ours {e_ours:.3e} eager {e_eager:.3e}; "
@@ -257,3 +265,27 @@ def test_flow_expert_euler(cuda):
     # 180 layer passes deep: the max-element statistic is noisy, the L2 one is not
     assert l2_ours <= max(1e-2, 1.1 * l2_eager)
     assert e_ours <= max(1e-2, 1.25 * e_eager)
+
+
+@pytest.mark.parametrize("t,s,masked", [(64, 3164, True), (96, 96, False), (1, 500, False)])
+def test_gqa_sdpa_attention_matches_transformers(cuda, t, s, masked):
+    """The attention the fused forward uses gives transformers' sdpa result without the
+    K/V head expansion (masked case: queries at the end of a longer key range)."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    class M(torch.nn.Module):
+        num_key_value_groups = 2
+        is_causal = True
+
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(2, 16, t, 128, generator=g).bfloat16().to(cuda)
+    k = torch.randn(2, 8, s, 128, generator=g).bfloat16().to(cuda)
+    v = torch.randn(2, 8, s, 128, generator=g).bfloat16().to(cuda)
+    mask = None
+    if masked:
+        mask = torch.ones(t, s, dtype=torch.bool, device=cuda).tril(diagonal=s - t)
+        mask = mask[None, None].expand(2, 1, t, s)
+    ref, _ = sdpa_attention_forward(M(), q, k, v, mask, scaling=128 ** -0.5)
+    got, _ = integrate.gqa_sdpa_attention(M(), q, k, v, mask, scaling=128 ** -0.5)
+    assert got.shape == ref.shape
+    assert oracle.rel_err(got, ref) <= 2e-3

@@ -14,7 +14,10 @@
 //              stage back to the producer through an mbarrier;
 //   warps 2-5  epilogue: tcgen05.ld of the fp32 accumulator (each warp reads
 //              its 32-lane TMEM quarter), bias / activation / residual in
-//              registers, bf16 stores.
+//              registers, then the bf16 32 x 32 chunk is staged in shared
+//              memory (64-byte swizzle, double-buffered per warp) and written
+//              with one TMA store, so output leaves in full lines instead of
+//              32 scattered 16-byte pieces per instruction.
 // The accumulator is double-buffered in TMEM (2 x 256 columns), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -57,7 +60,10 @@ struct Geo {
   static constexpr uint32_t kBBytes = kBN * kBK * 2 / kPair;  // B rows held by one CTA
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = kPair == 2 ? 6 : 4;
-  static constexpr size_t kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t kBarBytes = 1024;                       // barriers + flags
+  static constexpr uint32_t kStageOut = kStages * kStageBytes + kBarBytes;  // output staging
+  static constexpr uint32_t kOutBytes = 4 * 2 * 32 * 64;              // 4 warps x 2 x [32 x 32] bf16
+  static constexpr size_t kSmem = kStageOut + kOutBytes + 1024 /*align*/;
   static constexpr int kTileM = kBM * kPair;
   // D fp32, A/B bf16, both K-major, N = 256, M = 128 x kPair
   static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kBN >> 3) << 17) |
@@ -163,6 +169,11 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t a, const uint4& v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w) : "memory");
+}
+
 // 32 lanes x 32 consecutive fp32 columns; thread i receives lane (base + i).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -207,7 +218,8 @@ template <bool kDual, int kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b,
-                   const __grid_constant__ CUtensorMap map_b2, TcParams p) {
+                   const __grid_constant__ CUtensorMap map_b2,
+                   const __grid_constant__ CUtensorMap map_y, TcParams p) {
   using G = Geo<kPair>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -384,6 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ----------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    // two [32 rows x 32 cols] bf16 staging buffers per epilogue warp for TMA stores
+    const uint32_t stg0 = sbase + G::kStageOut + quarter * 4096;
+    int chunk_idx = 0;
     int it = 0;
     for (int t = unit; t < tiles; t += units, ++it) {
       int mb, nb;
@@ -413,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (kPair == 2) mbar_arrive_cluster(lead_acce0 + 8 * acc);
           else mbar_arrive(acce0 + 8 * acc);
         }
-        if (row >= p.m) continue;  // rows past m: no stores (TMA read zeros there)
+        const bool live = row < p.m;  // rows past m hold zeros; the TMA store clips them
         const int cbase = col0 + c;
         if (!kDual) {
           if (p.bias) {
@@ -434,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
           }
-          if (p.residual) {
+          if (p.residual && live) {
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
               if (cbase + i < p.n) {
@@ -446,18 +461,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        __nv_bfloat16* out = p.y + static_cast<int64_t>(row) * p.ldy + cbase;
+        // Stage the warp's 32 x 32 chunk (64-byte swizzle: 16-byte chunk j of row r at
+        // j ^ ((r >> 1) & 3), conflict-free) and store it with one TMA copy.
+        const uint32_t buf = stg0 + (chunk_idx & 1) * 2048;
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          if (cbase + i < p.n) {
-            float o[8];
+        for (int j = 0; j < 4; ++j) {
+          float o[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = v[i + j];
-            st_vec(out + i, pack8(o));
-          }
+          for (int jj = 0; jj < 8; ++jj) o[jj] = v[j * 8 + jj];
+          st_shared_v4(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4), pack8(o));
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_y, buf, cbase,
+                       mb * G::kTileM + static_cast<int>(rank) * kBM + quarter * 32);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        ++chunk_idx;
       }
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -533,7 +560,9 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   // A CTA pair (256-row tiles) whenever there is more than one 128-row block.
   const bool pair = m > kBM;
   const int b_rows = pair ? kBN / 2 : (kDual ? kBN / 2 : kBN);
-  CUtensorMap ma, mb, mb2;
+  CUtensorMap ma, mb, mb2, my;
+  if (!make_out_map(&my, y, m, n, ldy))
+    return fail(UMIC_ERR_DEVICE, "%s: output tensor map rejected", name);
   if (!make_map(&ma, x, m, k, ldx, kBM) || !make_map(&mb, w, n, k, ldw, b_rows) ||
       !make_map(&mb2, kDual ? w2 : w, n, k, kDual ? ldw2 : ldw, b_rows))
     return fail(UMIC_ERR_DEVICE, "%s: cuTensorMapEncodeTiled unavailable or rejected", name);
@@ -560,7 +589,7 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   if (!pair) {
     if (int rc = set_smem_attr<kDual, 1>()) return rc;
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-    tc_gemm_kernel<kDual, 1><<<grid, kThreads, Geo<1>::kSmem, st>>>(ma, mb, mb2, p);
+    tc_gemm_kernel<kDual, 1><<<grid, kThreads, Geo<1>::kSmem, st>>>(ma, mb, mb2, my, p);
     return launch_status(name);
   }
   if (int rc = set_smem_attr<kDual, 2>()) return rc;
@@ -577,7 +606,7 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<kDual, 2>, ma, mb, mb2, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<kDual, 2>, ma, mb, mb2, my, p);
   if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", name, cudaGetErrorString(e));
   return launch_status(name);
 }

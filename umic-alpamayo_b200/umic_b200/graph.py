@@ -15,7 +15,8 @@ Differences from the reference, all on the host side:
     position (no index_copy_), and the attention reads the buffer prefix as a
     view instead of a per-step contiguous copy;
   * FlowStepGraph (graph.py:179-253 of the reference, never wired there) is
-    provided and used by the flow workload.
+    provided and used by workloads.flow_sample(graph=True), which captures a
+    whole Euler step (expert pass + update) once and replays it.
 """
 
 from __future__ import annotations

@@ -223,13 +223,33 @@ def _fused_attention_forward(self, hidden_states, position_embeddings=None, atte
         keys, values = k4.transpose(1, 2), v4.transpose(1, 2)
         if past_key_values is not None:
             keys, values = past_key_values.update(keys, values, self.layer_idx)
-    attn = ALL_ATTENTION_FUNCTIONS.get_interface(self.config._attn_implementation,
-                                                 eager_attention_forward)
+    impl = self.config._attn_implementation
+    attn = (gqa_sdpa_attention if impl == "sdpa"
+            else ALL_ATTENTION_FUNCTIONS.get_interface(impl, eager_attention_forward))
     out, weights = attn(self, q4.transpose(1, 2), keys, values, attention_mask,
                         dropout=0.0 if not self.training else self.attention_dropout,
                         scaling=self.scaling, **kwargs)
     out = out.reshape(b, s, -1).contiguous()
     return self.o_proj(out), weights
+
+
+def gqa_sdpa_attention(module: nn.Module, query: torch.Tensor, key: torch.Tensor,
+                       value: torch.Tensor, attention_mask: torch.Tensor | None,
+                       dropout: float = 0.0, scaling: float | None = None,
+                       is_causal: bool | None = None, **kwargs):
+    """transformers' "sdpa" attention (same mask and causal rules) with SDPA's native
+    grouped-query path for every mask. transformers 5.x expands K/V to the query heads
+    (repeat_kv) whenever a mask is passed -- e.g. the flow expert's 64 action tokens
+    over a 3.1 k-token prefix, two ~0.4 GB copies per layer per step; SDPA with
+    enable_gqa takes the boolean mask directly (cuDNN kernel, same result)."""
+    if attention_mask is not None and attention_mask.dim() == 4:
+        attention_mask = attention_mask[:, :, :, : key.shape[-2]]
+    causal = is_causal if is_causal is not None else getattr(module, "is_causal", True)
+    causal = bool(query.shape[2] > 1 and attention_mask is None and causal)
+    out = nn.functional.scaled_dot_product_attention(
+        query, key, value, attn_mask=attention_mask, dropout_p=dropout, scale=scaling,
+        is_causal=causal, enable_gqa=query.shape[1] != key.shape[1])
+    return out.transpose(1, 2).contiguous(), None
 
 
 def fuse_attention(model: nn.Module, dry_run: bool = False) -> int:
