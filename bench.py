@@ -42,8 +42,9 @@ TOKENS = 3100
 LAYERS = 36
 HIDDEN, INTER = 4096, 12288
 # DRAM bytes (read + write) of one dual-GEMM launch at the 8-episode shape
-# (M = 24800), from `ncu --set full` (profiles/gemm_gate_silu_mul_cfg4_prefill.md).
-DUAL_GEMM_TRAFFIC_M24800 = 3.43e9
+# (M = 24800): 2.111 GB read + 0.608 GB written, from `ncu --set full` of the
+# CTA-pair kernel with the TMA-store epilogue (profiles/gemm_gate_silu_mul_cfg4_prefill.md).
+DUAL_GEMM_TRAFFIC_M24800 = 2.72e9
 
 
 def _peaks() -> dict:
