@@ -1,7 +1,7 @@
 // Shared pieces of the TMA-fed kernels (tensor-core GEMM, streaming GEMV):
 // mbarrier operations with bounded waits, 2-D TMA tile loads, and the host-side
-// tensor-map encoding of bf16 K-major operands. No load here uses cluster
-// multicast; every copy lands in the issuing CTA's own shared memory.
+// tensor-map encoding of bf16 K-major operands. Every load lands only in the
+// issuing CTA's own shared memory (no cluster-wide broadcast).
 #pragma once
 
 #include <cuda.h>
