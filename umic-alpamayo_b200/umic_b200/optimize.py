@@ -8,6 +8,8 @@ Additions, on by default and reported:
     q/k RMSNorm, RoPE, KV-cache write) runs as one kernel after the projections;
   * decode_gemv: every remaining LM / expert Linear runs the GEMV kernel when
     it sees fewer than FUSE_MIN_ROWS rows (the reference left those on cuBLAS);
+  * vision_gemm_fusion: the ViT MLPs run fc1 with the tanh-GELU in the GEMM
+    epilogue (the reference's epilogue was erf-only, so it kept them on cuBLAS);
   * the expert's MLPs and q/o projections take the same GEMMs as the LM;
   * the LM / expert lookups also accept the transformers 5.x layout, where the
     VLM holds its language model and vision tower under `.model`.
@@ -26,7 +28,7 @@ logger = logging.getLogger(__name__)
 @dataclasses.dataclass
 class UmicConfig:
     """Which optimizations to apply (defaults: the reference's adopted set,
-    src/umic/optimize.py:34-72, plus decode_gemv)."""
+    src/umic/optimize.py:34-72, plus the additions listed above)."""
 
     mlp_fusion: bool = True
     linear_fusion: bool = True
@@ -41,6 +43,7 @@ class UmicConfig:
     max_new_tokens: int = 96
     decode_gemv: bool = True
     attention_fusion: bool = True
+    vision_gemm_fusion: bool = True
 
 
 def _has_layers(m) -> bool:
@@ -110,6 +113,10 @@ def apply(model: nn.Module, config: UmicConfig | None = None) -> dict:
         report["ve_patch_embed_fused"] = integrate.fuse_patch_embed_linear(visual)
         report["ve_attn_varlen_fused"] = integrate.fuse_vision_attention_varlen(visual)
         report["ve_pipeline_fused"] = integrate.fuse_vision_encoder_pipeline(visual)
+        if cfg.vision_gemm_fusion:
+            # fc1 + tanh-GELU in one GEMM epilogue (the reference left the ViT MLPs on
+            # cuBLAS because its epilogue was erf-GELU, src/umic/integrate.py:93-95)
+            report["ve_gelu_mlp_fused"] = integrate.fuse_gelu_mlps(visual)
 
     expert = getattr(model, "expert", None)
     if expert is not None:
