@@ -332,11 +332,30 @@ def run_umic(args) -> None:
         }
         if eager and eager.get("ms_per_step"):
             line["speedup_vs_eager_gpu"] = eager["ms_per_step"] / ms_step
+        if world == 1 and not args.skip_extras:
+            line.update(_extras())
         print(json.dumps(line), flush=True)
     model._umic_decode_runner.release()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _extras() -> dict:
+    """cfg3 (ViT) and cfg5 (flow expert) timings from `python -m umic_b200.extras`, run
+    in a subprocess so their apply() patches stay out of this process."""
+    import subprocess
+
+    try:
+        res = subprocess.run([sys.executable, "-m", "umic_b200.extras"],
+                             cwd=str(ROOT / "umic-alpamayo_b200"), capture_output=True,
+                             text=True, timeout=900)
+        lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+        if res.returncode == 0 and lines:
+            return json.loads(lines[-1])
+        return {"extras_error": (res.stderr.strip().splitlines() or ["no output"])[-1][:300]}
+    except Exception as exc:  # noqa: BLE001 - a failed side measurement must not lose the line
+        return {"extras_error": str(exc)[:300]}
 
 
 def main() -> None:
@@ -348,6 +367,8 @@ def main() -> None:
     ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--skip-eager", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-extras", action="store_true",
+                    help="skip the cfg3 ViT and cfg5 flow timings (umic_b200.extras)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per launch of the dominant kernel, if measured")
     args = ap.parse_args()
