@@ -97,6 +97,44 @@ def main() -> None:
             ms = s0.elapsed_time(e0) / reps
             res[f"gemv_b2b_{name}_m8_{n}x{kd}"] = (ms, n * kd * 2 / (ms * 1e-3) / 1e9)
         del Ws
+    # The decode step's GEMV sequence as the decode graph runs it: 36 layers x (q/k/v in
+    # one launch, o_proj, gate+up gated, down_proj) + lm_head, x of 8 rows, captured in a
+    # CUDA graph and replayed; weights (15.1 GB) stream from HBM every replay.
+    from umic_b200.kernels.linear import linear_gemv_multi
+    layers = 36
+    mats = []
+    for _ in range(layers):
+        mats.append(dict(q=torch.randn(4096, 4096, device=dev, dtype=bf) * 0.02,
+                         k=torch.randn(1024, 4096, device=dev, dtype=bf) * 0.02,
+                         v=torch.randn(1024, 4096, device=dev, dtype=bf) * 0.02,
+                         o=torch.randn(4096, 4096, device=dev, dtype=bf) * 0.02,
+                         g=torch.randn(12288, 4096, device=dev, dtype=bf) * 0.02,
+                         u=torch.randn(12288, 4096, device=dev, dtype=bf) * 0.02,
+                         d=torch.randn(4096, 12288, device=dev, dtype=bf) * 0.02))
+    head = torch.randn(151936, 4096, device=dev, dtype=bf) * 0.02
+    chain_bytes = sum(sum(t.numel() for t in m_.values()) for m_ in mats) * 2 + head.numel() * 2
+    xs = torch.randn(8, 4096, device=dev, dtype=bf)
+
+    def step():
+        h = xs
+        for m_ in mats:
+            q, _, _ = linear_gemv_multi(h, [m_["q"], m_["k"], m_["v"]], weights_ready=True)
+            a = linear_gemv(q, m_["o"], weights_ready=True)
+            gu = gate_silu_mul_nk(a, m_["g"], m_["u"], weights_ready=True)
+            h = linear_gemv(gu, m_["d"], weights_ready=True)
+        return linear_gemv(h, head, weights_ready=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize()
+    ms = t(graph.replay, iters=10, flushl2=False)
+    res["decode_gemv_chain_m8"] = (ms, chain_bytes / (ms * 1e-3) / 1e9)
+    del mats, head, graph
     for kk_, v in res.items():
         print(kk_, v)
     if "--out" in sys.argv:
