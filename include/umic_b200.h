@@ -206,6 +206,18 @@ UMIC_API int umic_gemv_noalloc(const void* x, int64_t ldx, const void* w, int64_
                                const void* bias, void* y, int64_t ldy, int64_t m, int64_t n,
                                int64_t k, void* stream);
 
+/* umic_gemv with the residual add in its epilogue: y = x . w^T (+ bias) + res, with
+ * res [m, n] bf16 (leading dimension ldres, 16-byte aligned); y may be res itself
+ * (same pointer and leading dimension: each element is read before it is written). The
+ * streaming engine only (1 <= m <= 16, a workspace as for umic_gemv); other shapes
+ * return UMIC_ERR_UNSUPPORTED and the caller keeps its unfused path. Replaces, in a
+ * decode step, down_proj followed by the residual add (integrate.py:180-209, the
+ * decoder-layer forward whose tail this is, and the Linear it calls). */
+UMIC_API int umic_gemv_residual(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                const void* bias, const void* res, int64_t ldres, void* y,
+                                int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace,
+                                size_t workspace_bytes, uint32_t flags, void* stream);
+
 /* Bytes of workspace the streaming engine needs for `rows` weight rows in one call
  * (for umic_gemv_multi: the sum of n_i) on the current device. */
 UMIC_API size_t umic_gemv_workspace_bytes(int64_t rows);

@@ -355,6 +355,43 @@ def test_gemv_gated_streaming_repeatable(cuda):
     _close(h1, oracle.gate_silu_mul(x.cpu(), wg.cpu().t(), wu.cpu().t()))
 
 
+# ------------------------------------------- GEMV with the residual add in its epilogue
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_gemv_residual_epilogue(cuda, m):
+    from umic_b200.kernels.linear import linear_gemv_residual
+
+    h = _randn(m, 12288, seed=300, dev=cuda)
+    wd = _randn(4096, 12288, seed=301, dev=cuda, scale=0.02)
+    bias = _randn(4096, seed=304, dev=cuda)
+    res_in = _randn(m, 4096, seed=302, dev=cuda)
+    stats.clear()
+    out = linear_gemv_residual(h, wd, res_in, bias, weights_ready=True)
+    assert stats["umic_gemv_residual"] == 1 and stats["gemv_residual_fallback"] == 0
+    _close(out, oracle.linear(h.cpu(), wd.cpu(), bias.cpu()) + res_in.cpu().float())
+    # y may be the residual buffer itself
+    y = res_in.clone()
+    ws, ws_bytes = _lib.gemv_workspace(cuda, 4096)
+    _lib.call("umic_gemv_residual", cuda, h.data_ptr(), h.stride(0), wd.data_ptr(),
+              wd.stride(0), bias.data_ptr(), y.data_ptr(), y.stride(0), y.data_ptr(),
+              y.stride(0), m, 4096, 12288, ws, ws_bytes, 0)
+    assert torch.equal(y, out)
+
+
+def test_gemv_residual_outside_streaming_engine(cuda):
+    from umic_b200.kernels.linear import linear_gemv_residual
+
+    h = _randn(20, 12288, seed=303, dev=cuda)
+    wd = _randn(4096, 12288, seed=301, dev=cuda, scale=0.02)
+    res_in = _randn(20, 4096, seed=305, dev=cuda)
+    stats.clear()
+    out = linear_gemv_residual(h, wd, res_in)  # 20 rows: GEMV, then the add
+    assert stats["gemv_residual_fallback"] == 1 and stats["umic_gemv"] == 1
+    _close(out, oracle.linear(h.cpu(), wd.cpu()) + res_in.cpu().float())
+    with pytest.raises(ValueError):
+        linear_gemv_residual(h, wd, res_in[:8])
+
+
 # ------------------------------------------------------------------ GEMM
 
 def _gpu_ref_linear(x, w, bias=None, act=None, residual=None):

@@ -311,6 +311,9 @@ struct StreamArgs {
   unsigned* cnt;  // [row blocks], zero between calls (after the slots)
   uint32_t* err;
   int weights_ready;  // the weights may be read before the previous kernel completes
+  // Optional residual added in the epilogue of a single plain GEMV: y = W x + res.
+  const __nv_bfloat16* res;
+  int64_t ldres;
 };
 
 __device__ __forceinline__ int st_unit_begin(int c, const StreamArgs& a) {
@@ -459,6 +462,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
       } else {
         o = v;
         if (a.bias[si]) o += bf(a.bias[si][nrow]);
+        if (a.res) o += bf(a.res[mcol * a.ldres + nrow]);
       }
       a.y[si][mcol * a.ldy[si] + nrow] = __float2bfloat16_rn(o);
     };
@@ -555,7 +559,8 @@ __global__ void __launch_bounds__(kStThreads, 1)
 #pragma unroll
       for (int mc = 0; mc < MC; ++mc) {
         const int xr = mc * 8 + g;
-        xv[s][mc] = (kk < a.k && xr < a.m) ? ld_cached(a.x + xr * a.ldx + kk) : zero;
+        const bool live = kk < a.k && xr < a.m;
+        xv[s][mc] = live ? ld_cached(a.x + xr * a.ldx + kk) : zero;
       }
     }
     // Every consumer warp passes or fails the same waits, so none is left alone at a
@@ -611,7 +616,8 @@ bool stream_eligible(const GemvArgs& a) {
 
 template <int MC, bool kGated>
 int stream_launch(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes,
-                  uint32_t flags, cudaStream_t st, bool pdl = true) {
+                  uint32_t flags, cudaStream_t st, bool pdl = true,
+                  const StreamArgs* extra = nullptr) {
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -664,6 +670,10 @@ int stream_launch(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes
   s.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + stream_counter_offset());
   s.err = device_error_word();
   s.weights_ready = (flags & UMIC_GEMV_WEIGHTS_READY) ? 1 : 0;
+  if (extra) {  // residual epilogue
+    s.res = extra->res;
+    s.ldres = extra->ldres;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(s.ctas, 1, 1);
   cfg.blockDim = dim3(kStThreads, 1, 1);
@@ -851,6 +861,46 @@ int umic_gemv_noalloc(const void* x, int64_t ldx, const void* w, int64_t ldw, co
   // complete before any CTA reads a counter.
   return a.m <= 8 ? stream_launch<1, false>(kName, a, scratch, kStaticScratchBytes, 0, st, false)
                   : stream_launch<2, false>(kName, a, scratch, kStaticScratchBytes, 0, st, false);
+}
+
+int umic_gemv_residual(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+                       const void* res, int64_t ldres, void* y, int64_t ldy, int64_t m, int64_t n,
+                       int64_t k, void* workspace, size_t workspace_bytes, uint32_t flags,
+                       void* stream) {
+  static const char* kName = "umic_gemv_residual";
+  clear_error();
+  if (!res) return fail(UMIC_ERR_INVALID_ARG, "%s: res is null", kName);
+  if (int rc = check(kName, x, ldx, w, w, ldw, y, ldy, m, n, k)) return rc;
+  if (m == 0 || n == 0) return UMIC_OK;
+  if (m > 16)
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: m=%lld rows of x; 1..16 supported", kName,
+                (long long)m);
+  if (!aligned16(res) || ldres < n)
+    return fail(UMIC_ERR_ALIGNMENT, "%s: res must be 16-byte aligned with ldres >= n", kName);
+  if (!workspace)
+    return fail(UMIC_ERR_INVALID_ARG, "%s: needs a workspace (streaming engine)", kName);
+  if (flags & ~static_cast<uint32_t>(UMIC_GEMV_WEIGHTS_READY))
+    return fail(UMIC_ERR_INVALID_ARG, "%s: unknown flags 0x%x", kName, flags);
+  GemvArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.ldx = ldx;
+  a.seg[0] = Seg{static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(bias),
+                 static_cast<__nv_bfloat16*>(y), ldw, ldy, 0, static_cast<int>(n)};
+  a.nseg = 1;
+  a.m = static_cast<int>(m);
+  a.n = static_cast<int>(n);
+  a.k = static_cast<int>(k);
+  a.slabs = static_cast<int>((k + 31) / 32);
+  if (!stream_eligible(a))
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: shape outside the streaming engine", kName);
+  StreamArgs extra{};
+  extra.res = static_cast<const __nv_bfloat16*>(res);
+  extra.ldres = ldres;
+  cudaStream_t st = as_stream(stream);
+  return a.m <= 8 ? stream_launch<1, false>(kName, a, workspace, workspace_bytes, flags, st, true,
+                                            &extra)
+                  : stream_launch<2, false>(kName, a, workspace, workspace_bytes, flags, st, true,
+                                            &extra);
 }
 
 size_t umic_gemv_workspace_bytes(int64_t rows) {

@@ -52,6 +52,8 @@ _SIGNATURES: dict[str, list] = {
                         ctypes.POINTER(_c_i64), ctypes.POINTER(_c_p), ctypes.POINTER(_c_p),
                         ctypes.POINTER(_c_i64), _c_i64, _c_i64, _c_p, _c_size, _c_u32, _c_p],
     "umic_gemv_workspace_bytes": [_c_i64],
+    "umic_gemv_residual": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64,
+                           _c_i64, _c_i64, _c_p, _c_size, _c_u32, _c_p],
     "umic_gemv_noalloc": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64,
                           _c_i64, _c_p],
     "umic_qk_norm_rope_kv": [_c_p, _c_i64, _c_i64, _c_i64, _c_i32, _c_p, _c_i64, _c_i64, _c_i64,

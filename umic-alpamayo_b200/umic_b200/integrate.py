@@ -28,7 +28,7 @@ from torch import nn
 from .kernels import rope as _rope
 from .kernels.fused_ffn import gate_silu_mul_nk
 from .kernels.layernorm import add_layernorm, layernorm
-from .kernels.linear import linear, linear_gemv
+from .kernels.linear import linear, linear_gemv, linear_gemv_residual
 from .kernels.rmsnorm import add_rmsnorm, rmsnorm
 
 logger = logging.getLogger(__name__)
@@ -71,9 +71,12 @@ def _is_p5_mlp(module: nn.Module) -> bool:
 
 
 def _project(lin: nn.Linear, x2d: torch.Tensor, residual: torch.Tensor | None = None):
-    """A Linear on the B200 kernels: GEMV below FUSE_MIN_ROWS, tcgen05 GEMM above."""
-    if x2d.shape[0] < FUSE_MIN_ROWS and residual is None:
-        return linear_gemv(x2d, lin.weight, lin.bias, weights_ready=True)
+    """A Linear on the B200 kernels: GEMV below FUSE_MIN_ROWS, tcgen05 GEMM above; a
+    residual is added in either kernel's epilogue."""
+    if x2d.shape[0] < FUSE_MIN_ROWS:
+        if residual is None:
+            return linear_gemv(x2d, lin.weight, lin.bias, weights_ready=True)
+        return linear_gemv_residual(x2d, lin.weight, residual, lin.bias, weights_ready=True)
     return linear(x2d, lin.weight, lin.bias, residual=residual)
 
 
@@ -82,8 +85,8 @@ def mlp_forward(mlp: nn.Module, x: torch.Tensor,
     """down(silu(gate(x)) * up(x)) [+ residual], x [..., H].
 
     gate/up run as one fused kernel (dual-accumulator GEMM or gated GEMV); the
-    down projection runs on the GEMM (with the residual add in its epilogue when
-    `residual` is given) or the GEMV below FUSE_MIN_ROWS.
+    down projection runs on the GEMM, or the GEMV below FUSE_MIN_ROWS, with the
+    residual add in its epilogue when `residual` is given.
     """
     shape = x.shape
     x2d = x.reshape(-1, shape[-1])
@@ -304,8 +307,8 @@ def _fused_residual_layer_forward(self, hidden_states, position_embeddings=None,
                                   use_cache=False, **kwargs):
     """Decoder layer with the attention residual folded into post_attention_layernorm
     (src/umic/integrate.py:180-209). When the MLP is P5-fused, its residual add
-    also moves into the down-projection epilogue (the reference left that add
-    eager, integrate.py:207-208)."""
+    also moves into the down-projection epilogue, of the GEMM or (decode rows) the
+    GEMV (the reference left that add eager, integrate.py:207-208)."""
     residual = hidden_states
     hidden_states = self.input_layernorm(hidden_states)
     hidden_states, _ = self.self_attn(
@@ -317,9 +320,7 @@ def _fused_residual_layer_forward(self, hidden_states, position_embeddings=None,
                                           _eps_of(self.post_attention_layernorm))
     mlp = self.mlp
     if getattr(mlp, "_umic_p5", False) and mlp.forward.__func__ is _fused_mlp_forward:
-        rows = hidden_states.numel() // hidden_states.shape[-1]
-        if rows >= FUSE_MIN_ROWS:
-            return mlp_forward(mlp, hidden_states, residual=residual)
+        return mlp_forward(mlp, hidden_states, residual=residual)
     hidden_states = mlp(hidden_states)
     return residual + hidden_states
 

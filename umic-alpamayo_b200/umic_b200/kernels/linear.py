@@ -129,3 +129,34 @@ def linear_gemv_multi(x2d: torch.Tensor, weights: list[torch.Tensor],
 
 # Name of the reference interface (src/umic/kernels/linear.py:118).
 linear_triton = linear
+
+
+
+def linear_gemv_residual(x2d: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor,
+                         bias: torch.Tensor | None = None, *,
+                         weights_ready: bool = False) -> torch.Tensor:
+    """y = x2d @ weight.T + bias + residual in one streaming-GEMV launch, the residual
+    add in the epilogue (C ABI: umic_gemv_residual); x2d has at most 16 rows. Shapes
+    outside the streaming engine run the GEMV and the add as two ops."""
+    dev = require_cuda("linear_gemv_residual", x2d, weight, residual, bias)
+    require_bf16("linear_gemv_residual", x2d, weight, residual, bias)
+    m, k = x2d.shape
+    n = weight.shape[0]
+    if residual.shape != (m, n):
+        raise ValueError(f"linear_gemv_residual: residual {tuple(residual.shape)} != {(m, n)}")
+    x2d = _k_major(x2d)
+    weight = _k_major(weight)
+    residual = _k_major(residual)
+    y = torch.empty((m, n), device=x2d.device, dtype=x2d.dtype)
+    ws, ws_bytes = _lib.gemv_workspace(dev, n)
+    rc = _lib.ERR_UNSUPPORTED
+    if m <= 16 and ws is not None:
+        rc = _lib.try_call("umic_gemv_residual", dev, x2d.data_ptr(), row_stride(x2d),
+                           weight.data_ptr(), row_stride(weight), _lib.ptr(bias),
+                           residual.data_ptr(), row_stride(residual), y.data_ptr(), n, m, n, k,
+                           ws, ws_bytes, _lib.GEMV_WEIGHTS_READY if weights_ready else 0)
+    if rc:
+        stats["gemv_residual_fallback"] += 1
+        return linear_gemv(x2d, weight, bias, weights_ready=weights_ready) + residual
+    stats["umic_gemv_residual"] += 1
+    return y
