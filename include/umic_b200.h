@@ -192,16 +192,25 @@ UMIC_API int umic_gemv(const void* x, int64_t ldx, const void* w, int64_t ldw, c
                        void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, void* workspace,
                        size_t workspace_bytes, uint32_t flags, void* stream);
 
-/* umic_gemv without a caller workspace and without any allocation: the streaming
- * engine runs on a scratch array that is part of the library image (a
- * 256-byte-aligned __device__ array of 4 MB + 64 KB per device, found once per
- * device with cudaGetSymbolAddress). Limits: 1 <= m <= 16, n <= 1048576 weight
- * rows, at most 256 SMs; larger calls return UMIC_ERR_UNSUPPORTED with the limit
- * in the message. Each call first clears its row-block counters with a
+/* umic_gemv without a caller workspace and without any allocation. No counterpart
+ * in the reference (its GEMVs go through torch, which allocates freely); this is an
+ * extra entry for hosts that cannot allocate device memory when they call in: an
+ * embedded driving stack that reserves all device memory at start-up and forbids
+ * cudaMalloc inside its real-time control loop (cudaMalloc and cudaFree may
+ * synchronise the device and have unbounded latency), or an FFI binding whose
+ * runtime owns device memory in its own pool and has no way to hand a workspace
+ * through. The streaming engine runs on a scratch array that is part of the
+ * library image: a 256-byte-aligned __device__ array of 4 MB + 64 KB that every
+ * GPU which loads the library holds until the process exits. Its device address
+ * is looked up with cudaGetSymbolAddress by the first call on each device (with
+ * that device current); make that first call before any stream capture.
+ * Limits: 1 <= m <= 16, n <= 1048576 weight rows, at most 256 SMs; larger calls
+ * return UMIC_ERR_UNSUPPORTED with the limit in the message. The array keeps the
+ * last call's contents, so each call first clears its row-block counters with a
  * stream-ordered cudaMemsetAsync and then launches in plain stream order. All
- * calls on one device share the array: calls that overlap in time (other streams
- * or threads) race on it and must be serialised by the caller. Same result as
- * umic_gemv with a workspace, bit for bit. */
+ * calls on one device share the array: calls that overlap on the GPU (other
+ * streams or threads) race on it and must be serialised by the caller. Same
+ * result as umic_gemv with a workspace, bit for bit. */
 UMIC_API int umic_gemv_noalloc(const void* x, int64_t ldx, const void* w, int64_t ldw,
                                const void* bias, void* y, int64_t ldy, int64_t m, int64_t n,
                                int64_t k, void* stream);

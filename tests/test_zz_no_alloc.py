@@ -1,6 +1,12 @@
 """The allocation-free GEMV entry point (umic_gemv_noalloc) against the workspace
 entry point (umic_gemv) it mirrors.
 
+umic_gemv_noalloc is for hosts that cannot allocate device memory when they call
+in -- an embedded control loop that reserved its memory at start-up and may not
+call cudaMalloc (it can synchronise the device and has no latency bound), or an FFI
+runtime that owns its device pool -- so its scratch is a static device array that
+lives in the library image.
+
 This file is collected last, so the scratch array is exercised both in a fresh
 process (run the file alone) and after every other GPU test has used the device.
 The two entry points run the same streaming kernel over the same unit partition,

@@ -694,9 +694,14 @@ int stream_launch(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes
 //
 // umic_gemv_noalloc runs the streaming engine on a scratch area that is part of
 // the library image: a file-scope __device__ array, created with the module on
-// each device, so the call itself allocates nothing. Its size bounds the calls it
-// takes (rows per call and SMs per device). One array per device serves every
-// such call on that device, from any stream or thread: overlapping calls race.
+// each device, so the call itself allocates nothing. It serves hosts that may not
+// allocate device memory at call time (a real-time control loop that reserved its
+// memory at start-up, an FFI runtime that owns its device pool). Its size bounds
+// the calls it takes (rows per call and SMs per device). One array per device
+// serves every such call on that device, from any stream or thread: calls that
+// overlap on the GPU race. Host code may not pass g_gemv_scratch itself to a
+// kernel (its host-side name is a stand-in, not a device address); the address
+// comes from cudaGetSymbolAddress, on the first call on each device.
 constexpr int64_t kStaticMaxRows = int64_t{1} << 20;
 constexpr int kStaticMaxSms = 256;
 constexpr size_t kStaticScratchBytes =
