@@ -167,6 +167,41 @@ UMIC_API int umic_qk_norm_rope_kv(
     int64_t pos, const int64_t* dpos, int64_t batch, int64_t seq, int32_t head_dim,
     void* stream);
 
+/* ---- attention over a cached prefix -------------------------------------- */
+
+/* out = softmax(scale * q . k^T, masked) . v with grouped-query heads, for few
+ * query rows per KV head over a long key prefix (the flow expert's action tokens
+ * over its cached prefix). q [batch, hq, t, 128] through strides (q_sb, q_sh,
+ * q_st); k, v [batch, hkv, lk, 128] through (sb, sh, sl) -- e.g. the prefix view of
+ * an in-place cache buffer; out [batch, hq, t, 128] through (o_sb, o_sh, o_st).
+ * mask_bits: the mask as packed by umic_mask_pack_bits -- key k of (b, head, token)
+ * attends iff bit k % 32 of word b*m_sb + head*m_sh + token*m_st + k / 32 is set (word
+ * strides; 0 broadcasts) -- or NULL for no mask; rows that attend to nothing come
+ * out as zeros. Covers head_dim 128, hq a multiple of hkv, (hq / hkv) * t <= 128 and
+ * t a multiple of 8, 16-byte aligned bases and strides that are multiples of 8
+ * elements; other shapes return UMIC_ERR_UNSUPPORTED / UMIC_ERR_ALIGNMENT and the
+ * caller keeps its own attention. No kernel counterpart in the reference: it leaves
+ * this attention to torch SDPA inside the HF attention forward that its flow-cache
+ * hook serves (src/umic/integrate.py:715-756); this replaces that SDPA call. */
+UMIC_API int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
+                                 const void* k, int64_t k_sb, int64_t k_sh, int64_t k_sl,
+                                 const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sl,
+                                 const uint32_t* mask_bits, int64_t m_sb, int64_t m_sh,
+                                 int64_t m_st, void* out, int64_t o_sb, int64_t o_sh,
+                                 int64_t o_st, int64_t batch, int64_t hq, int64_t hkv, int64_t t,
+                                 int64_t lk, int64_t head_dim, float scale, void* stream);
+
+/* Packs a boolean attention mask (bytes, nonzero = attend; element (b, h, token, key)
+ * at b*sb + h*sh + token*st + key) into bits for umic_attention_rows: word w of row
+ * (b, h, token), at bits + b*wb + h*wh + token*wt (word strides), holds keys
+ * 32 w .. 32 w + 31, key 32 w + i in bit i; bits past lk are zero. Each row needs
+ * ceil(lk / 32) words. Part of umic_attention_rows's path, no reference counterpart
+ * (the reference hands the byte mask to torch SDPA). */
+UMIC_API int umic_mask_pack_bits(const void* mask, int64_t sb, int64_t sh, int64_t st,
+                                 int64_t batch, int64_t heads, int64_t t, int64_t lk,
+                                 uint32_t* bits, int64_t wb, int64_t wh, int64_t wt,
+                                 void* stream);
+
 /* ---- projections (src/umic/kernels/linear.py, fused_ffn.py) -------------- */
 
 /* Row-count regime below FUSE_MIN_ROWS (integrate.py:27-30): HBM-bound GEMV,

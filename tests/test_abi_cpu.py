@@ -78,3 +78,33 @@ def test_kernel_wrappers_refuse_cpu_tensors():
         rmsnorm(x, torch.ones(8, dtype=torch.bfloat16), 1e-6)
     with pytest.raises(RuntimeError, match="no CPU path"):
         linear(x, torch.zeros(8, 8, dtype=torch.bfloat16))
+
+
+def test_attention_rows_rejects_uncovered_shapes_on_host():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(16)  # never dereferenced: the shape check fails first
+    # head_dim 80, and 2 x 72 = 144 query rows per KV head, are declined before any launch
+    assert L.umic_attention_rows(fake, 0, 0, 0, fake, 0, 0, 0, fake, 0, 0, 0, None, 0, 0, 0,
+                                 fake, 0, 0, 0, 1, 4, 2, 8, 64, 80, ctypes.c_float(0.1),
+                                 None) == 2
+    assert "128 only" in _lib.last_message()
+    assert L.umic_attention_rows(fake, 0, 0, 0, fake, 0, 0, 0, fake, 0, 0, 0, None, 0, 0, 0,
+                                 fake, 0, 0, 0, 1, 16, 8, 72, 64, 128, ctypes.c_float(0.1),
+                                 None) == 2
+    assert "144 query rows" in _lib.last_message()
+    # empty work returns at once
+    assert L.umic_attention_rows(None, 0, 0, 0, None, 0, 0, 0, None, 0, 0, 0, None, 0, 0, 0,
+                                 None, 0, 0, 0, 0, 16, 8, 64, 64, 128, ctypes.c_float(0.1),
+                                 None) == 0
+
+
+def test_binding_arity_matches_header():
+    """Every ctypes signature has as many arguments as the header's declaration (a
+    missing trailing stream would reach the runtime as a truncated integer)."""
+    text = HEADER.read_text()
+    for name, args in _lib._SIGNATURES.items():
+        m = re.search(r"UMIC_API\s+(?:int|size_t|const char\*)\s+" + name + r"\(([^;]*)\);",
+                      text, re.S)
+        assert m, name
+        params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
+        assert len(params) == len(args), f"{name}: header {len(params)} vs binding {len(args)}"

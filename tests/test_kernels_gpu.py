@@ -459,5 +459,95 @@ def test_gemm_repeat_deterministic(cuda):
     assert torch.equal(a, b)
 
 
+# --------------------------------------------- attention over a cached prefix
+
+def _attn_ref(q, k, v, mask, scale):
+    """fp32 softmax(scale q k^T, masked) v with grouped heads -> [B, T, Hq, D]; rows
+    that attend to nothing are zeros (the kernel's convention)."""
+    g = q.shape[1] // k.shape[1]
+    kf = k.float().repeat_interleave(g, 1)
+    vf = v.float().repeat_interleave(g, 1)
+    s = (q.float() @ kf.transpose(-1, -2)) * scale
+    if mask is not None:
+        s = s.masked_fill(~mask[..., : k.shape[2]], float("-inf"))
+    p = torch.nan_to_num(torch.softmax(s, -1), nan=0.0)
+    return (p @ vf).transpose(1, 2)
+
+
+@pytest.mark.parametrize("b,hq,hkv,t,lk,cap,kind", [
+    (4, 16, 8, 64, 3164, 3172, "lower_right"),  # the flow expert's step (4 episodes)
+    (2, 32, 8, 32, 1000, 1000, "lower_right"),  # 4 query heads per KV head, 128 rows
+    (3, 8, 8, 16, 100, 128, None),              # no mask, keys not a multiple of 64
+    (2, 16, 8, 64, 64, 64, "lower_right"),      # one block: plain causal
+    (2, 16, 8, 64, 700, 704, "random"),         # arbitrary mask, some rows see nothing
+    (2, 4, 2, 8, 200, 200, "per_head"),         # a mask per query head
+])
+def test_attention_rows(cuda, b, hq, hkv, t, lk, cap, kind):
+    from umic_b200.kernels.attention import attention_rows
+
+    d = 128
+    q = _randn(b, t, hq, d, seed=90, dev=cuda).transpose(1, 2)  # HF's [B, Hq, T, D] view
+    kbuf = _randn(b, hkv, cap, d, seed=91, dev=cuda)
+    vbuf = _randn(b, hkv, cap, d, seed=92, dev=cuda)
+    k, v = kbuf[:, :, :lk], vbuf[:, :, :lk]  # prefix views of cache buffers
+    mask = None
+    if kind == "lower_right":
+        mask = torch.ones(t, lk, dtype=torch.bool, device=cuda).tril(diagonal=lk - t)
+        mask = mask[None, None].expand(b, 1, t, lk)
+    elif kind == "random":
+        g = torch.Generator(device="cpu").manual_seed(93)
+        mask = (torch.rand(b, 1, t, lk + 5, generator=g) > 0.3).to(cuda)
+        mask[0, 0, 3] = False  # a row with no visible key
+    elif kind == "per_head":
+        g = torch.Generator(device="cpu").manual_seed(94)
+        mask = (torch.rand(b, hq, t, lk, generator=g) > 0.5).to(cuda)
+        mask[..., 0] = True
+    scale = d ** -0.5
+    stats.clear()
+    out = attention_rows(q, k, v, mask, scale)
+    assert out is not None and stats["umic_attention_rows"] == 1
+    assert out.shape == (b, t, hq, d)
+    ref = _attn_ref(q, k, v, mask, scale)
+    _close(out, ref)
+    if kind != "random":  # torch SDPA (bf16) on the same inputs, for scale
+        sdpa = torch.nn.functional.scaled_dot_product_attention(
+            q, k, v, attn_mask=mask, scale=scale, enable_gqa=True).transpose(1, 2)
+        e_ours, e_sdpa = oracle.rel_err(out, ref), oracle.rel_err(sdpa, ref)
+        print(f"attention_rows {kind}: l2 vs fp32 ours {e_ours:.2e}, torch sdpa {e_sdpa:.2e}")
+        assert e_ours <= max(2e-3, 1.5 * e_sdpa)
+    assert torch.equal(out, attention_rows(q, k, v, mask, scale))  # deterministic
+    if kind == "random":
+        assert float(out[0, 3].float().abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("b,h,t,lk", [(2, 1, 64, 3164), (1, 3, 5, 32), (3, 2, 7, 33), (1, 1, 1, 1)])
+def test_mask_pack_bits(cuda, b, h, t, lk):
+    g = torch.Generator(device="cpu").manual_seed(99)
+    mask = (torch.rand(b, h, t, lk + 3, generator=g) > 0.5).to(cuda)
+    words = (lk + 31) // 32
+    bits = torch.full((b, h, t, words), -1, device=cuda, dtype=torch.int32)
+    _lib.call("umic_mask_pack_bits", cuda, mask.data_ptr(), mask.stride(0), mask.stride(1),
+              mask.stride(2), b, h, t, lk, bits.data_ptr(), bits.stride(0), bits.stride(1),
+              bits.stride(2))
+    m = torch.zeros(b, h, t, words * 32, dtype=torch.int64)
+    m[..., :lk] = mask[..., :lk].cpu().long()
+    ref = (m.view(b, h, t, words, 32) << torch.arange(32)).sum(-1)
+    got = bits.cpu().long() & 0xFFFFFFFF
+    assert torch.equal(got, ref)
+
+
+def test_attention_rows_declines_uncovered_shapes(cuda):
+    from umic_b200.kernels.attention import attention_rows
+
+    q = _randn(1, 16, 100, 128, seed=95, dev=cuda)  # 2 x 100 rows per KV head > 128
+    k = _randn(1, 8, 300, 128, seed=96, dev=cuda)
+    stats.clear()
+    assert attention_rows(q, k, k, None, 0.1) is None
+    q80 = _randn(1, 4, 8, 80, seed=97, dev=cuda)  # head_dim 80
+    k80 = _randn(1, 2, 64, 80, seed=98, dev=cuda)
+    assert attention_rows(q80, k80, k80, None, 0.1) is None
+    assert stats["attention_rows_fallback"] == 2 and stats["umic_attention_rows"] == 0
+
+
 def test_no_device_error_after_suite(cuda):
     assert _lib.device_errors(cuda, clear=True) == 0

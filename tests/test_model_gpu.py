@@ -251,6 +251,7 @@ def test_flow_expert_euler(cuda):
                          x0.bfloat16())
     assert stats["umic_gemm_gate_silu_mul"] == 18 * 10
     assert stats["umic_qk_norm_rope_kv"] == 18 * 10  # KV write fused into the attention prep
+    assert stats["umic_attention_rows"] == 18 * 10  # masked prefix attention on tcgen05
     # the same 10 steps with one captured Euler step replayed: 2 eager warm-up steps, one
     # side-stream pass before capture and the capture itself go through Python; the 8
     # replays launch the same kernels from the graph
@@ -288,6 +289,8 @@ def test_gqa_sdpa_attention_matches_transformers(cuda, t, s, masked):
         mask = torch.ones(t, s, dtype=torch.bool, device=cuda).tril(diagonal=s - t)
         mask = mask[None, None].expand(2, 1, t, s)
     ref, _ = sdpa_attention_forward(M(), q, k, v, mask, scaling=128 ** -0.5)
+    stats.clear()
     got, _ = integrate.gqa_sdpa_attention(M(), q, k, v, mask, scaling=128 ** -0.5)
+    assert stats["umic_attention_rows"] == (1 if masked else 0)
     assert got.shape == ref.shape
     assert oracle.rel_err(got, ref) <= 2e-3

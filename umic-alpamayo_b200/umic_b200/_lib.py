@@ -60,6 +60,12 @@ _SIGNATURES: dict[str, list] = {
                              _c_p, _c_i64, _c_i64, _c_i64, _c_i32, _c_p, _c_p, _c_int, _c_f32,
                              _c_f32, _c_p, _c_p, _c_i64, _c_i64, _c_int, _c_p, _c_p, _c_i64,
                              _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i32, _c_p],
+    "umic_attention_rows": [_c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p,
+                            _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
+                            _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                            _c_f32, _c_p],
+    "umic_mask_pack_bits": [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
+                            _c_i64, _c_i64, _c_i64, _c_p],
     "umic_gemm": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64,
                   _c_i64, _c_int, _c_p],
     "umic_gemm_gate_silu_mul": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64,

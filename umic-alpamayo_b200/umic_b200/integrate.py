@@ -244,9 +244,21 @@ def gqa_sdpa_attention(module: nn.Module, query: torch.Tensor, key: torch.Tensor
     grouped-query path for every mask. transformers 5.x expands K/V to the query heads
     (repeat_kv) whenever a mask is passed -- e.g. the flow expert's 64 action tokens
     over a 3.1 k-token prefix, two ~0.4 GB copies per layer per step; SDPA with
-    enable_gqa takes the boolean mask directly (cuDNN kernel, same result)."""
+    enable_gqa takes the boolean mask directly (cuDNN kernel, same result). A boolean
+    mask over few query rows per KV head (at most 128, e.g. 64 action tokens x 2
+    query heads) goes to the tcgen05 kernel (kernels.attention.attention_rows)."""
     if attention_mask is not None and attention_mask.dim() == 4:
         attention_mask = attention_mask[:, :, :, : key.shape[-2]]
+        if (attention_mask.dtype == torch.bool and query.shape[2] > 1 and dropout == 0.0
+                and query.is_cuda and query.dtype == torch.bfloat16):
+            # Few query rows per KV head over a long prefix (the flow expert's action
+            # tokens over the cached prefix): the tcgen05 kernel reads the mask itself.
+            from .kernels.attention import attention_rows
+
+            out = attention_rows(query, key, value, attention_mask,
+                                 scaling if scaling is not None else query.shape[-1] ** -0.5)
+            if out is not None:
+                return out, None
     causal = is_causal if is_causal is not None else getattr(module, "is_causal", True)
     causal = bool(query.shape[2] > 1 and attention_mask is None and causal)
     out = nn.functional.scaled_dot_product_attention(

@@ -13,6 +13,9 @@ Used to capture a single kernel under ncu. Modes and shapes:
   rope_vision    q, k [16384, 16, 80] views of qkv, fp32 tables     (cfg2d)
   gemv           x [rows=8, 4096], W [12288, 4096]
   kv             K/V [8, 8, 3100, 128] appended into [8, 8, 3172, 128]
+  attn           flow-step attention: q [rows=32 episodes, 16, 64, 128] over the
+                 3164-key prefix of a [32, 8, 3172, 128] cache, lower-right causal mask
+                 (mask packing + umic_attention_rows)
 Inputs are seeded random tensors created on cuda:0 before the launches.
 """
 
@@ -82,6 +85,17 @@ def make(mode: str, rows: int | None):
         x = torch.randn(rows or 8, 4096, device=dev, dtype=bf)
         w = torch.randn(12288, 4096, device=dev, dtype=bf)
         return lambda: linear_gemv(x, w)
+    if mode == "attn":
+        from .kernels.attention import attention_rows
+
+        b, hq, hk, t, lk, cap, d = (rows or 32), 16, 8, 64, 3164, 3172, 128
+        q = torch.randn(b, t, hq, d, device=dev, dtype=bf).transpose(1, 2)
+        kb = torch.randn(b, hk, cap, d, device=dev, dtype=bf)
+        vb = torch.randn_like(kb)
+        mask = torch.ones(t, lk, dtype=torch.bool, device=dev).tril(diagonal=lk - t)
+        mask = mask[None, None].expand(b, 1, t, lk).contiguous()
+        k, v = kb[:, :, :lk], vb[:, :, :lk]
+        return lambda: attention_rows(q, k, v, mask, d ** -0.5)
     if mode == "kv":
         kb = torch.zeros(8, 8, 3172, 128, device=dev, dtype=bf)
         vb = torch.zeros_like(kb)

@@ -1,9 +1,13 @@
-"""Attention-input preparation on the B200 kernel (C ABI: umic_qk_norm_rope_kv).
+"""Attention on the B200 kernels (C ABI: umic_qk_norm_rope_kv, umic_attention_rows).
 
-One launch does what the HF attention forward (transformers qwen3_vl
-Qwen3VLTextAttention.forward) runs as four steps after the projections:
+qk_norm_rope_kv: one launch does what the HF attention forward (transformers
+qwen3_vl Qwen3VLTextAttention.forward) runs as four steps after the projections:
 q_norm / k_norm per head, apply_rotary_pos_emb, and the KV-cache write
 (past_key_values.update -> InplaceLayer.update, src/umic/cache.py:50-80).
+
+attention_rows: the attention itself for few query rows per KV head over a long
+cached prefix under a boolean mask -- the flow expert's action tokens over the
+prefix KV, which torch's SDPA sends to an sm80-generation cuDNN kernel.
 """
 
 from __future__ import annotations
@@ -65,3 +69,54 @@ def qk_norm_rope_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor | None,
             raise RuntimeError(str(e).split(": ", 1)[-1]) from None
         raise
     stats["umic_qk_norm_rope_kv"] += 1
+
+
+def attention_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   mask: torch.Tensor | None, scale: float) -> torch.Tensor | None:
+    """softmax(scale * q k^T, masked) v with grouped-query heads, on the tcgen05 kernel.
+
+    q [B, Hq, T, D], k / v [B, Hkv, Lk, D] (any strides, D contiguous), mask a bool
+    tensor broadcastable to [B, Hq, T, >= Lk] (True = attend) or None; the mask is
+    packed to bits first (umic_mask_pack_bits, one launch). Returns
+    [B, T, Hq, D] (the layout transformers' attention functions return), or None
+    when the kernel does not cover the shape (head_dim 128, Hq / Hkv * T <= 128
+    query rows per KV head, T a multiple of 8) so the caller keeps its own path.
+    """
+    dev = require_cuda("attention_rows", q, k, v, mask)
+    require_bf16("attention_rows", q, k, v)
+    bsz, hq, t, d = q.shape
+    hkv, lk = k.shape[1], k.shape[2]
+    if k.shape != v.shape or k.shape[0] != bsz or k.shape[3] != d:
+        raise ValueError(f"attention_rows: q {tuple(q.shape)} / k {tuple(k.shape)} / "
+                         f"v {tuple(v.shape)}")
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        return None
+    bits, ws = None, (0, 0, 0)
+    if mask is not None:
+        if mask.dtype != torch.bool or mask.dim() != 4 or mask.shape[-1] < lk:
+            return None
+        if mask.shape[1] not in (1, hq) or mask.shape[0] not in (1, bsz) or \
+                mask.shape[2] not in (1, t):
+            return None
+        if mask.stride(-1) != 1:
+            mask = mask.contiguous()
+        hm, words = mask.shape[1], (lk + 31) // 32
+        bits = torch.empty(mask.shape[0], hm, mask.shape[2], words, device=dev,
+                           dtype=torch.int32)
+        _lib.call("umic_mask_pack_bits", dev, mask.data_ptr(), mask.stride(0),
+                  mask.stride(1), mask.stride(2), mask.shape[0], hm, mask.shape[2], lk,
+                  bits.data_ptr(), bits.stride(0), bits.stride(1), bits.stride(2))
+        stats["umic_mask_pack_bits"] += 1
+        ws = (bits.stride(0) if bits.shape[0] > 1 else 0, bits.stride(1) if hm > 1 else 0,
+              bits.stride(2) if bits.shape[2] > 1 else 0)
+    out = torch.empty(bsz, t, hq, d, device=dev, dtype=q.dtype)
+    rc = _lib.try_call("umic_attention_rows", dev, q.data_ptr(), q.stride(0), q.stride(1),
+                       q.stride(2), k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+                       v.data_ptr(), v.stride(0), v.stride(1), v.stride(2), _lib.ptr(bits),
+                       ws[0], ws[1], ws[2], out.data_ptr(), out.stride(0), out.stride(2),
+                       out.stride(1), bsz, hq, hkv, t, lk, d, float(scale))
+    if rc:
+        stats["attention_rows_fallback"] += 1
+        return None
+    stats["umic_attention_rows"] += 1
+    return out
