@@ -289,8 +289,12 @@ def test_gqa_sdpa_attention_matches_transformers(cuda, t, s, masked):
         mask = torch.ones(t, s, dtype=torch.bool, device=cuda).tril(diagonal=s - t)
         mask = mask[None, None].expand(2, 1, t, s)
     ref, _ = sdpa_attention_forward(M(), q, k, v, mask, scaling=128 ** -0.5)
+    ref32, _ = sdpa_attention_forward(M(), q.float(), k.float(), v.float(), mask,
+                                      scaling=128 ** -0.5)
     stats.clear()
     got, _ = integrate.gqa_sdpa_attention(M(), q, k, v, mask, scaling=128 ** -0.5)
     assert stats["umic_attention_rows"] == (1 if masked else 0)
     assert got.shape == ref.shape
-    assert oracle.rel_err(got, ref) <= 2e-3
+    # two bf16 computations of the same attention, each ~2e-3 from fp32
+    assert oracle.rel_err(got, ref32) <= 1.25 * oracle.rel_err(ref, ref32) + 1e-4
+    assert oracle.rel_err(got, ref) <= 5e-3

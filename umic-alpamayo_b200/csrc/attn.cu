@@ -7,26 +7,31 @@
 // (umic_mask_pack_bits packs the boolean mask: one 32-bit word per 32 keys, so a
 // thread reads two words per block instead of 64 scattered bytes). One CTA per
 // (batch, kv head) holds its G * T query rows as one M = 128 tile and streams the
-// keys and values through a 5-stage ring of 64-key blocks. Per block:
+// keys and values through a 5-stage ring of 64-key blocks. Per block j:
 //   S = Q K^T               tcgen05.mma M128 N64 K128 into TMEM (K-major operands);
-//   P = exp2(S' - m)        eight warps, two per query row: each thread takes 32
-//                           of a row's 64 keys (the pair swaps row maxima through
-//                           shared memory), keeps the running max m (online
-//                           softmax), rounds P to bf16 and writes it over the
-//                           block's K slot (the K block is dead once S is
-//                           computed); the running sum l adds the rounded values,
-//                           so the weights applied to V sum to 1;
-//   O = alpha * O + P V     O accumulates in TMEM across blocks; V is the
-//                           MN-major operand (d contiguous), so no transpose is
-//                           made; O is rescaled in place only in warps whose
-//                           running max moved (after the first blocks, almost none).
-// The MMA for S of block j+1 runs while the softmax warps work on block j.
-// At the end each thread divides its row by l and writes it as bf16.
+//   P = exp2(S' - m)        softmax warp group j % 2, one query row per thread:
+//                           mask, scale, running max m and sum l of the group's
+//                           blocks (online softmax), P rounded to bf16 and written
+//                           over the block's K slot (the K block is dead once S is
+//                           computed); l adds the rounded values, so the weights
+//                           applied to V sum to 1;
+//   O_g = alpha O_g + P V   into the group's own TMEM accumulator (V is the
+//                           MN-major operand, d contiguous, so no transpose is
+//                           made); the reference max moves, and O_g is rescaled
+//                           in place, only when a row's max grows by more than 8
+//                           in log2 units (weights stay <= 256), i.e. rarely.
+// The two groups (warps 2-5 and 6-9, one of each on every SM sub-partition) run
+// independent chains on alternate blocks and exchange nothing until the end, where
+// each row's two partial results are merged with their maxima and sums. The MMA
+// for S of block j + 2 is issued as soon as group j % 2 has read S of block j, so
+// it runs while the group works on block j.
 //
-// HBM-bound at the flow shape (every K/V byte is read once: 415 MB per layer for
-// 32 episodes x 8 KV heads x 3164 keys): one CTA per SM keeps 160 KB of K/V in
-// flight (a 2-stage ring at two CTAs per SM left each block waiting on its load),
-// and two softmax warps per SM sub-partition hide each other's latencies.
+// Every K/V byte is read once (415 MB per layer for 32 episodes x 8 KV heads x 3164
+// keys at the flow shape). A slot of the ring is refilled only after the P V of its
+// block, and a block's load takes ~3 us to land under this traffic, so each slot
+// turns over about every 5 us: the ring, not HBM, sets the pace (about 1 us per
+// block per CTA, 0.5-0.6 of the HBM bound; six stages or an L2 prefetch of each slot's
+// next block measured no faster).
 //
 // Every mbarrier wait is bounded; a wait that runs out sets
 // UMIC_DEVERR_WAIT_TIMEOUT, the CTA lets its copies land, drains its MMAs, frees
@@ -46,14 +51,16 @@ constexpr int kD = 128;        // head dim
 constexpr int kRows = 128;     // query rows per CTA (TMEM lanes)
 constexpr int kKeys = 64;      // keys per block
 constexpr int kStages = 5;
+// S of block j + 2 is issued before P V of block j, whose stage the ring refills:
+// with fewer than three stages the ring could not hold block j + 2 yet.
+static_assert(kStages >= 3, "the MMA issuer runs two blocks ahead of the P V MMAs");
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 softmax
 constexpr uint32_t kQBytes = kRows * kD * 2;          // 32 KB: two 16 KB atom columns
 constexpr uint32_t kKBytes = kKeys * kD * 2;          // 16 KB: two 8 KB atom columns
 constexpr uint32_t kStageBytes = 2 * kKBytes;         // K (later P) + V
 constexpr uint32_t kBarOff = kQBytes + kStages * kStageBytes;
-constexpr uint32_t kXchOff = kBarOff + 256;          // row maxima / sums exchanged
-constexpr size_t kSmem = kXchOff + 2 * 2 * kRows * 4 + 1024;  // [parity][half][row], align
-constexpr uint32_t kTmemCols = 256;                   // S: cols 0-63, O: cols 128-255
+constexpr size_t kSmem = kBarOff + 256 + 1024;        // barriers and flags, alignment
+constexpr uint32_t kTmemCols = 512;  // S_0, S_1: cols 0-63, 64-127; O_0, O_1: 128-255, 256-383
 constexpr uint32_t kTmemO = 128;
 
 // kind::f16 instruction descriptors: D fp32, A/B bf16, M = 128.
@@ -127,6 +134,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 64 consecutive fp32 columns in one load and one wait (the softmax reads a
+// whole block's scores per thread; two 32-column loads would pay two round trips).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -155,6 +176,21 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Non-blocking check that the phase with the given parity has completed
+// (mbarrier.try_wait may suspend the thread for a while when it has not, which would
+// hold up the MMA issuer's other work).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t a, const uint4& v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
@@ -178,14 +214,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  // q_full, kv_full[kStages], kv_empty[kStages], s_full, s_empty, p_full, o_full, drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6 + 2 * kStages);
+  // q_full, kv_full[kStages], kv_empty[kStages], s_full[2], s_empty[2], p_full[2][2],
+  // o_full[2], o_last, drain
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13 + 2 * kStages);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t q_full = smem_u32(bars), kv_full0 = q_full + 8;
   const uint32_t kv_empty0 = kv_full0 + 8 * kStages, s_full = kv_empty0 + 8 * kStages;
-  const uint32_t s_empty = s_full + 8, p_full = s_full + 16, o_full = s_full + 24;
-  const uint32_t drain = s_full + 32;
+  // Per softmax group g: s_full[g] (S of its next block is in TMEM), s_empty[g] (the
+  // group has read it), p_full[g][n & 1] (P of the group's n-th block is in shared
+  // memory; two barriers, as the group may finish its next block before the issuer
+  // looks), o_full[g] (P V of its block landed in O_g). o_last: every MMA done (the
+  // final read of O_0 and O_1).
+  const uint32_t s_empty0 = s_full + 16, p_full0 = s_full + 32, o_full0 = s_full + 64;
+  const uint32_t o_last = s_full + 80, drain = s_full + 88;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.x / p.hkv, h = blockIdx.x % p.hkv;
   const uint32_t qs = sbase;
@@ -198,10 +240,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(kv_full0 + 8 * s, 1);
       mbar_init(kv_empty0 + 8 * s, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, 256);
-    mbar_init(p_full, 256);
-    mbar_init(o_full, 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full + 8 * g, 1);
+      mbar_init(s_empty0 + 8 * g, 128);
+      mbar_init(p_full0 + 16 * g, 128);
+      mbar_init(p_full0 + 16 * g + 8, 128);
+      mbar_init(o_full0 + 8 * g, 1);
+    }
+    mbar_init(o_last, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -245,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_4d(kslot(s) + half * (kKBytes / 2), &map_k, fb, half * 64, j * kKeys, h, b);
           tma_load_4d(vslot(s) + half * (kKBytes / 2), &map_v, fb, half * 64, j * kKeys, h, b);
         }
+
       }
       if (ok) {
         // The last stages are released by the MMA before the CTA may exit.
@@ -261,192 +308,245 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t tmem_s = tmem_base, tmem_o = tmem_base + kTmemO;
-      auto issue_s = [&](int s) {
+      auto issue_s = [&](int s, int g) {
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           // d step of 16 = 32 bytes inside an atom column; columns are 16 KB (Q) / 8 KB (K) apart
           const uint32_t qa = qs + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32;
           const uint32_t ka = kslot(s) + (kk >> 2) * (kKBytes / 2) + (kk & 3) * 32;
-          mma(tmem_s, sdesc(qa, 16, 1024), sdesc(ka, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+          mma(tmem_base + 64 * g, sdesc(qa, 16, 1024), sdesc(ka, 16, 1024), kIdescS,
+              kk > 0 ? 1u : 0u);
         }
+        commit(s_full + 8 * g);
       };
-      bool ok = mbar_wait(q_full, 0, p.err, abort_flag) &&
-                mbar_wait(kv_full0, 0, p.err, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-        commit(s_full);
-      }
-      for (int j = 0; ok && j < p.nblk; ++j) {
-        const int s = j % kStages;
-        if (j + 1 < p.nblk) {
-          // S of the next block as soon as its keys are in and S_j has been read.
-          const int s1 = (j + 1) % kStages;
-          if (!mbar_wait(kv_full0 + 8 * s1, ((j + 1) / kStages) & 1, p.err, abort_flag) ||
-              !mbar_wait(s_empty, j & 1, p.err, abort_flag)) {
-            ok = false;
-            break;
-          }
+      auto kv_ready = [&](int j) {
+        return mbar_wait(kv_full0 + 8 * (j % kStages), (j / kStages) & 1, p.err, abort_flag);
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, abort_flag);
+      for (int j = 0; ok && j < 2 && j < p.nblk; ++j) {
+        ok = kv_ready(j);
+        if (ok) {
           tc_fence_after();
-          issue_s(s1);
-          commit(s_full);
+          issue_s(j % kStages, j);
         }
-        if (!mbar_wait(p_full, j & 1, p.err, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kKeys / 16; ++kk) {
-          // P: one 128-row atom column, key step of 16 = 32 bytes. V (MN-major): key
-          // step of 16 = two 8-key groups of 1024 bytes; d halves 8 KB apart.
-          const uint32_t pa = kslot(s) + kk * 32;
-          const uint32_t va = vslot(s) + kk * 2048;
-          mma(tmem_o, sdesc(pa, 16, 1024), sdesc(va, kKBytes / 2, 1024), kIdescPV,
-              (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        commit(o_full);
-        commit(kv_empty0 + 8 * s);  // K/P and V slots free for block j + kStages
       }
+      // Event loop: issue whichever is ready -- S of block ns (its group has read S of
+      // block ns - 2, its keys are in) or P V of block npv (its group wrote P) -- so
+      // neither group waits behind the other. S runs at most three blocks ahead of P V
+      // (ns < npv + 4), so a group can be at most one of its own blocks past the one
+      // whose P this thread waits for (hence two p_full barriers per group), and every
+      // other barrier at most at the phase waited for: every parity wait stays exact.
+      int ns = p.nblk < 2 ? p.nblk : 2, npv = 0;
+      const long long t0 = clock64();
+      for (uint32_t spin = 0; ok && npv < p.nblk;) {
+        bool progressed = false;
+        if (ns < p.nblk && ns < npv + 4) {
+          const int g = ns & 1, n = (ns - 2) >> 1;
+          if (mbar_test(s_empty0 + 8 * g, n & 1) &&
+              mbar_test(kv_full0 + 8 * (ns % kStages), (ns / kStages) & 1)) {
+            tc_fence_after();
+            issue_s(ns % kStages, g);
+            ++ns;
+            progressed = true;
+          }
+        }
+        {
+          const int g = npv & 1, s = npv % kStages, n = npv >> 1;
+          if (mbar_test(p_full0 + 16 * g + 8 * (n & 1), (n >> 1) & 1)) {
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kKeys / 16; ++kk) {
+              // P: one 128-row atom column, key step of 16 = 32 bytes. V (MN-major): key
+              // step of 16 = two 8-key groups of 1024 bytes; d halves 8 KB apart.
+              const uint32_t pa = kslot(s) + kk * 32;
+              const uint32_t va = vslot(s) + kk * 2048;
+              mma(tmem_base + kTmemO + 128 * g, sdesc(pa, 16, 1024),
+                  sdesc(va, kKBytes / 2, 1024), kIdescPV, (npv >= 2 || kk > 0) ? 1u : 0u);
+            }
+            commit(o_full0 + 8 * g);
+            commit(kv_empty0 + 8 * s);  // K/P and V slots free for block npv + kStages
+            ++npv;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          spin = 0;
+        } else if ((++spin & 255u) == 0) {
+          if (*abort_flag) {
+            ok = false;
+          } else if (clock64() - t0 > kWaitLimitCycles) {
+            *abort_flag = 1;
+            if (p.err) atomicOr(p.err, UMIC_DEVERR_WAIT_TIMEOUT);
+            ok = false;
+          }
+        }
+      }
+      if (ok) commit(o_last);
       commit(drain);
       mbar_wait(drain, 0, p.err, abort_flag);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------- softmax
-    // Warps w and w + 4 share TMEM lanes 32 * (w % 4), i.e. 32 query rows: half 0
-    // takes keys 0-31 of each block and O columns 0-63, half 1 keys 32-63 and O
-    // columns 64-127. Both pass or fail the same waits, so neither is left alone
-    // at their named barrier.
+    // Group g = warps 2-5 (g 0) or 6-9 (g 1) takes blocks j = g, g + 2, ...; warp w
+    // reads TMEM lanes 32 * (w % 4), i.e. query rows 32 * (w % 4) .. + 31. Both
+    // groups pass or fail the same final waits, so neither is left alone at the
+    // named barrier where they merge.
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int grp = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const bool valid = r < p.g * p.t;
     const int g = valid ? r / p.t : 0, t = valid ? r % p.t : 0;
     const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t ts = tmem_base + lanes + 32 * half;
-    const uint32_t to = tmem_base + lanes + kTmemO + 64 * half;
-    float* xch = reinterpret_cast<float*>(smem + kXchOff);  // [parity][half][row]
-    const uint32_t pair_bar = 1 + quarter;
-    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory"); };
+    const uint32_t ts = tmem_base + lanes + 64 * grp;
+    const uint32_t to0 = tmem_base + lanes + kTmemO;  // O_0; O_1 is 128 columns on
+    const uint32_t to = to0 + 128 * grp;
     const uint32_t* mrow =
         p.bits ? p.bits + b * p.m_sb + (h * p.g + g) * p.m_sh + t * p.m_st : nullptr;
     const int words = (p.lk + 31) >> 5;
-    // this block's mask word (keys 32 * half .. + 31), loaded one block ahead
-    uint32_t w = 0xffffffffu;
-    if (mrow && valid) w = half < words ? __ldg(mrow + half) : 0u;
+    // the mask words of the group's current block, loaded one block ahead
+    uint32_t w0 = 0xffffffffu, w1 = 0xffffffffu;
+    if (mrow && valid) {
+      w0 = 2 * grp < words ? __ldg(mrow + 2 * grp) : 0u;
+      w1 = 2 * grp + 1 < words ? __ldg(mrow + 2 * grp + 1) : 0u;
+    }
     const float ninf = -INFINITY, sl2 = p.scale_log2;
     float m_run = ninf, l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < p.nblk; ++j) {
-      if (!mbar_wait(s_full, j & 1, p.err, abort_flag)) {
+    for (int j = grp, n = 0; j < p.nblk; j += 2, ++n) {
+      if (!mbar_wait(s_full + 8 * grp, n & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[32];
-      tmem_ld32(ts, sv);
+      float sv[64];
+      tmem_ld64(ts, sv);
+      float* s0 = sv;
+      float* s1 = sv + 32;
       tc_fence_before();
-      mbar_arrive(s_empty);
+      mbar_arrive(s_empty0 + 8 * grp);  // S_g may take the group's next block now
       // keys past Lk are cut by index (their bits, if any, are padding)
-      const int left = p.lk - (j * kKeys + 32 * half);
-      const uint32_t lim = left >= 32 ? 0xffffffffu : (left > 0 ? (1u << left) - 1u : 0u);
-      const uint32_t mw = valid ? (w & lim) : 0u;
+      const int left = p.lk - j * kKeys;
+      const uint32_t lim0 = left >= 32 ? 0xffffffffu : (left > 0 ? (1u << left) - 1u : 0u);
+      const uint32_t lim1 = left >= 64 ? 0xffffffffu : (left > 32 ? (1u << (left - 32)) - 1u : 0u);
+      const uint32_t m0 = valid ? (w0 & lim0) : 0u, m1 = valid ? (w1 & lim1) : 0u;
       if (mrow && valid) {
-        const int wi = 2 * j + 2 + half;
-        w = wi < words ? __ldg(mrow + wi) : 0u;
+        const int wi = 2 * (j + 2);
+        w0 = wi < words ? __ldg(mrow + wi) : 0u;
+        w1 = wi + 1 < words ? __ldg(mrow + wi + 1) : 0u;
       }
-      if (!__all_sync(0xffffffffu, mw == 0xffffffffu)) {  // masked keys in this warp's block
+      if (!__all_sync(0xffffffffu, (m0 & m1) == 0xffffffffu)) {  // masked keys in this block
 #pragma unroll
-        for (int c = 0; c < 32; ++c) sv[c] = (mw >> c) & 1u ? sv[c] : ninf;
+        for (int c = 0; c < 32; ++c) {
+          s0[c] = (m0 >> c) & 1u ? s0[c] : ninf;
+          s1[c] = (m1 >> c) & 1u ? s1[c] : ninf;
+        }
       }
       // tree reductions keep the dependent chains short
-      float mx[16];
+      float mx[32];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) mx[c] = fmaxf(sv[c], sv[c + 16]);
+      for (int c = 0; c < 32; ++c) mx[c] = fmaxf(s0[c], s1[c]);
 #pragma unroll
-      for (int w2 = 8; w2 >= 1; w2 >>= 1)
+      for (int w2 = 16; w2 >= 1; w2 >>= 1)
 #pragma unroll
         for (int c = 0; c < w2; ++c) mx[c] = fmaxf(mx[c], mx[c + w2]);
-      float mb = mx[0];
-      float* xj = xch + (j & 1) * 2 * kRows;
-      xj[half * kRows + r] = mb;
-      pair_sync();
-      mb = fmaxf(mb, xj[(half ^ 1) * kRows + r]);
-      // raw scores are scaled inside the exponent: p = 2^(s * scale * log2 e - m')
-      const float m_new = fmaxf(m_run, mb);
+      // Raw scores are scaled inside the exponent: p = 2^(s * scale * log2 e - m').
+      // The reference max m' moves only when the block's max exceeds it by more than
+      // 8 (in log2 units): below that the weights stay <= 256, and O and l share the
+      // stale reference, so the final O / l is unchanged while O is rescaled far less
+      // often.
+      const bool move = m_run == ninf || (mx[0] - m_run) * sl2 > 8.f;
+      const float m_new = move ? fmaxf(m_run, mx[0]) : m_run;
       const float m_use = m_new == ninf ? 0.f : m_new;
-      const float alpha = ex2((m_run - m_use) * sl2);
+      const float alpha = move ? ex2((m_run - m_use) * sl2) : 1.f;
       const float msc = m_use * sl2;
-      float ps[16];
-      uint32_t pk[16];
+      float ps[32];
+      uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 32; c += 2) {
-        const __nv_bfloat162 pb = __floats2bfloat162_rn(ex2(fmaf(sv[c], sl2, -msc)),
-                                                        ex2(fmaf(sv[c + 1], sl2, -msc)));
+        const __nv_bfloat162 pa = __floats2bfloat162_rn(ex2(fmaf(s0[c], sl2, -msc)),
+                                                        ex2(fmaf(s0[c + 1], sl2, -msc)));
+        const __nv_bfloat162 pb = __floats2bfloat162_rn(ex2(fmaf(s1[c], sl2, -msc)),
+                                                        ex2(fmaf(s1[c + 1], sl2, -msc)));
         // the row sum of the rounded weights the MMA uses, so they sum to exactly 1
-        const float2 f = __bfloat1622float2(pb);
-        ps[c / 2] = f.x + f.y;
-        pk[c / 2] = *reinterpret_cast<const uint32_t*>(&pb);
+        const float2 fa = __bfloat1622float2(pa), fb = __bfloat1622float2(pb);
+        ps[c / 2] = fa.x + fa.y;
+        ps[16 + c / 2] = fb.x + fb.y;
+        pk[c / 2] = *reinterpret_cast<const uint32_t*>(&pa);
+        pk[16 + c / 2] = *reinterpret_cast<const uint32_t*>(&pb);
       }
 #pragma unroll
-      for (int w2 = 8; w2 >= 1; w2 >>= 1)
+      for (int w2 = 16; w2 >= 1; w2 >>= 1)
 #pragma unroll
         for (int c = 0; c < w2; ++c) ps[c] += ps[c + w2];
-      l_run = l_run * alpha + ps[0];  // this half's share of the row sum
+      l_run = l_run * alpha + ps[0];
       m_run = m_new;
-      if (j > 0) {
-        // O holds blocks < j at the old max: wait for P_{j-1} V_{j-1}, then rescale
-        // this warp's 64 columns if some row's max moved.
-        if (!mbar_wait(o_full, (j - 1) & 1, p.err, abort_flag)) {
+      if (n > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O_g holds the group's earlier blocks at the old max: wait for the last of
+        // them (phase n - 1 of o_full[g]), then rescale. Without a rescale the wait is
+        // skipped. S_j was issued after the P V of block j - 4 (S stays less than four
+        // blocks ahead of P V), so s_full already implies phase n - 2 completed, and
+        // block j's own P V is not issued yet: o_full[g] is at phase n - 1 or just past
+        // it, never further.
+        if (!mbar_wait(o_full0 + 8 * grp, (n - 1) & 1, p.err, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < 64; c += 32) {
-            float o[32];
-            tmem_ld32(to + c, o);
+        for (int c = 0; c < kD; c += 32) {
+          float o[32];
+          tmem_ld32(to + c, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(to + c, o);
-          }
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(to + c, o);
         }
       }
-      // P_j over this block's K slot: row r, 16-byte chunk c8 at r * 128 + (c8 ^ (r & 7)) * 16;
-      // this half writes chunks 4 * half .. 4 * half + 3.
+      // P_j over this block's K slot: row r, 16-byte chunk c8 at r * 128 + (c8 ^ (r & 7)) * 16.
       const uint32_t pbase = kslot(j % kStages) + r * 128;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        st_shared_v4(pbase + (((4 * half + i) ^ (r & 7)) << 4),
-                     make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
+      for (int c8 = 0; c8 < 8; ++c8)
+        st_shared_v4(pbase + ((c8 ^ (r & 7)) << 4),
+                     make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]));
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(p_full0 + 16 * grp + 8 * (n & 1));
     }
-    if (ok && mbar_wait(o_full, (p.nblk - 1) & 1, p.err, abort_flag)) {
+    if (ok && mbar_wait(o_last, 0, p.err, abort_flag)) {
       tc_fence_after();
-      // whole-row sum: the two halves meet in the exchange buffer the last block left free
-      float* xl = xch + (p.nblk & 1) * 2 * kRows;
-      xl[half * kRows + r] = l_run;
-      pair_sync();
-      const float l = l_run + xl[(half ^ 1) * kRows + r];
+      // merge the two groups' partial rows: common max, weights, whole-row sum (the
+      // exchange uses stage 0's K slot: every load and MMA has completed by now)
+      float* xm = reinterpret_cast<float*>(smem + kQBytes);  // [group][row]
+      float* xl = xm + 2 * kRows;
+      xm[grp * kRows + r] = m_run;
+      xl[grp * kRows + r] = l_run;
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+      const float ma = xm[r], mb2 = xm[kRows + r];
+      const float mm = fmaxf(ma, mb2);
+      const float mu = mm == ninf ? 0.f : mm;
+      const float sa = ex2((ma - mu) * sl2), sb = ex2((mb2 - mu) * sl2);
+      const float l = xl[r] * sa + xl[kRows + r] * sb;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow =
-          p.out + b * p.o_sb + (h * p.g + g) * p.o_sh + t * p.o_st + 64 * half;
+      const bool two = p.nblk > 1;  // O_1 holds data only if group 1 had a block
+      __nv_bfloat16* orow = p.out + b * p.o_sb + (h * p.g + g) * p.o_sh + t * p.o_st + 64 * grp;
 #pragma unroll 1
-      for (int c = 0; c < 64; c += 32) {
-        float o[32];
-        tmem_ld32(to + c, o);
+      for (int c = 64 * grp; c < 64 * grp + 64; c += 32) {
+        float oa[32], ob[32];
+        tmem_ld32(to0 + c, oa);
+        if (two) {
+          tmem_ld32(to0 + 128 + c, ob);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ob[i] = 0.f;
+        }
         if (valid) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             float f[8];
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) f[jj] = o[i + jj] * inv;
-            st_vec(orow + c + i, pack8(f));
+            for (int jj = 0; jj < 8; ++jj)
+              f[jj] = (oa[i + jj] * sa + ob[i + jj] * sb) * inv;
+            st_vec(orow + (c - 64 * grp) + i, pack8(f));
           }
         }
       }
@@ -479,10 +579,19 @@ __global__ void __launch_bounds__(256) mask_pack_kernel(const uint8_t* __restric
   const int64_t bi = rest / hm;
   const uint8_t* src = mask + bi * sb + hi * sh + ti * st;
   uint32_t* dst = bits + bi * wb + hi * wh + ti * wt;
-  for (int w = 0; w < (lk + 31) >> 5; ++w) {
-    const int key = w * 32 + lane;
-    const uint32_t word = __ballot_sync(0xffffffffu, key < lk && src[key] != 0);
-    if (lane == 0) dst[w] = word;
+  const int words = (lk + 31) >> 5;
+  for (int w0 = 0; w0 < words; w0 += 8) {
+    uint8_t v[8];  // eight independent loads in flight before the ballots
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int key = (w0 + i) * 32 + lane;
+      v[i] = key < lk ? src[key] : 0;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t word = __ballot_sync(0xffffffffu, v[i] != 0);
+      if (lane == 0 && w0 + i < words) dst[w0 + i] = word;
+    }
   }
 }
 
