@@ -16,6 +16,7 @@ tests/test_oracle_golden.py.
 from .formulas import (  # noqa: F401
     add_layernorm,
     add_rmsnorm,
+    attention,
     gate_silu_mul,
     layernorm,
     linear,

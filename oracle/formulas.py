@@ -119,3 +119,23 @@ def swiglu_block(x, residual, norm_w, eps, w_gate_nk, w_up_nk, w_down_nk):
     normed, summed = add_rmsnorm(x, residual, norm_w, eps)
     h = silu(normed @ _f(w_gate_nk).t()) * (normed @ _f(w_up_nk).t())
     return summed + h @ _f(w_down_nk).t()
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor | None,
+              scale: float) -> torch.Tensor:
+    """softmax(scale * q k^T, masked) v in fp32 with grouped-query heads -> [B, T, Hq, D].
+
+    The attention transformers runs for the patched Qwen3 attention (sdpa_attention_forward
+    in transformers/integrations/sdpa_attention.py: repeat_kv over the query heads, then
+    torch SDPA with the boolean mask, True = attend), which the reference leaves in
+    place. q [B, Hq, T, D], k / v [B, Hkv, L, D], mask broadcastable to [B, Hq, T, L].
+    Rows that attend to nothing come out as zeros."""
+    qf, kf, vf = _f(q), _f(k), _f(v)
+    g = qf.shape[1] // kf.shape[1]
+    kf = kf.repeat_interleave(g, 1)
+    vf = vf.repeat_interleave(g, 1)
+    s = (qf @ kf.transpose(-1, -2)) * scale
+    if mask is not None:
+        s = s.masked_fill(~mask.detach().cpu()[..., : kf.shape[2]], float("-inf"))
+    p = torch.nan_to_num(torch.softmax(s, -1), nan=0.0)
+    return (p @ vf).transpose(1, 2)

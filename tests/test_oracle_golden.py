@@ -123,3 +123,25 @@ def test_kv_cache_oracle_replays_reference_sequence(gv):
                 z = torch.zeros(c["k0"].shape[0], c["k0"].shape[1], 5, c["k0"].shape[3])
                 ref.update(z, z)
             assert str(e.value) == st["message"]
+
+
+def test_attention_oracle_matches_transformers_sdpa():
+    """oracle.attention against the attention transformers runs for the patched Qwen3
+    attention (sdpa_attention_forward: repeat_kv + torch SDPA), on CPU in fp32, with the
+    flow expert's mask (new tokens over a cached prefix) and without a mask."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    class M(torch.nn.Module):
+        num_key_value_groups = 2
+        is_causal = True
+
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(2, 16, 24, 128, generator=g)
+    k = torch.randn(2, 8, 200, 128, generator=g)
+    v = torch.randn(2, 8, 200, 128, generator=g)
+    mask = torch.ones(24, 200, dtype=torch.bool).tril(diagonal=200 - 24)[None, None]
+    mask = mask.expand(2, 1, 24, 200)
+    for m in (mask, None):
+        ref, _ = sdpa_attention_forward(M(), q, k, v, m, scaling=128 ** -0.5, is_causal=False)
+        got = oracle.attention(q, k, v, m, 128 ** -0.5)
+        assert oracle.rel_err(got, ref) < 1e-5

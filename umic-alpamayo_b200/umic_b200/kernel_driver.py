@@ -1,6 +1,6 @@
 """Runs one kernel of the library a few times on a BASELINE shape (profiling driver).
 
-    python -m umic_b200.kernel_driver <mode> [rows] [--iters N]
+    python -m umic_b200.kernel_driver <mode> [rows] [--iters N] [--time]
 
 Used to capture a single kernel under ncu. Modes and shapes:
   dual           gate/up dual-accumulator GEMM, x [rows=24800, 4096], W [12288, 4096] x 2
@@ -16,7 +16,11 @@ Used to capture a single kernel under ncu. Modes and shapes:
   attn           flow-step attention: q [rows=32 episodes, 16, 64, 128] over the
                  3164-key prefix of a [32, 8, 3172, 128] cache, lower-right causal mask
                  (mask packing + umic_attention_rows)
-Inputs are seeded random tensors created on cuda:0 before the launches.
+  attn_nomask    the same without a mask
+  attn_sdpa      the same shape and mask through torch SDPA (what transformers runs)
+Inputs are seeded random tensors created on cuda:0 before the launches. --time runs
+3 warm-up launches and then times --iters launches back to back with CUDA events
+(the inputs of the attention modes exceed L2), printing microseconds per launch.
 """
 
 from __future__ import annotations
@@ -85,7 +89,7 @@ def make(mode: str, rows: int | None):
         x = torch.randn(rows or 8, 4096, device=dev, dtype=bf)
         w = torch.randn(12288, 4096, device=dev, dtype=bf)
         return lambda: linear_gemv(x, w)
-    if mode == "attn":
+    if mode in ("attn", "attn_nomask", "attn_sdpa"):
         from .kernels.attention import attention_rows
 
         b, hq, hk, t, lk, cap, d = (rows or 32), 16, 8, 64, 3164, 3172, 128
@@ -95,6 +99,11 @@ def make(mode: str, rows: int | None):
         mask = torch.ones(t, lk, dtype=torch.bool, device=dev).tril(diagonal=lk - t)
         mask = mask[None, None].expand(b, 1, t, lk).contiguous()
         k, v = kb[:, :, :lk], vb[:, :, :lk]
+        if mode == "attn_nomask":
+            return lambda: attention_rows(q, k, v, None, d ** -0.5)
+        if mode == "attn_sdpa":
+            return lambda: torch.nn.functional.scaled_dot_product_attention(
+                q, k, v, attn_mask=mask, scale=d ** -0.5, enable_gqa=True)
         return lambda: attention_rows(q, k, v, mask, d ** -0.5)
     if mode == "kv":
         kb = torch.zeros(8, 8, 3172, 128, device=dev, dtype=bf)
@@ -110,8 +119,22 @@ def main() -> None:
     ap.add_argument("mode")
     ap.add_argument("rows", nargs="?", type=int, default=None)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--time", action="store_true")
     a = ap.parse_args()
     fn = make(a.mode, a.rows)
+    if a.time:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(a.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        print(f"{a.mode}: {s.elapsed_time(e) * 1e3 / a.iters:.1f} us per launch "
+              f"({a.iters} back to back)")
+        return
     for _ in range(a.iters):
         fn()
     torch.cuda.synchronize()
