@@ -83,11 +83,11 @@ def test_kernel_wrappers_refuse_cpu_tensors():
 def test_attention_rows_rejects_uncovered_shapes_on_host():
     L = _lib.lib()
     fake = ctypes.c_void_p(16)  # never dereferenced: the shape check fails first
-    # head_dim 80, and 2 x 72 = 144 query rows per KV head, are declined before any launch
+    # head_dim 48, and 2 x 72 = 144 query rows per KV head, are declined before any launch
     assert L.umic_attention_rows(fake, 0, 0, 0, fake, 0, 0, 0, fake, 0, 0, 0, None, 0, 0, 0,
-                                 fake, 0, 0, 0, 1, 4, 2, 8, 64, 80, ctypes.c_float(0.1),
+                                 fake, 0, 0, 0, 1, 4, 2, 8, 64, 48, ctypes.c_float(0.1),
                                  None) == 2
-    assert "128 only" in _lib.last_message()
+    assert "64..128" in _lib.last_message()
     assert L.umic_attention_rows(fake, 0, 0, 0, fake, 0, 0, 0, fake, 0, 0, 0, None, 0, 0, 0,
                                  fake, 0, 0, 0, 1, 16, 8, 72, 64, 128, ctypes.c_float(0.1),
                                  None) == 2

@@ -474,18 +474,20 @@ def _attn_ref(q, k, v, mask, scale):
     return (p @ vf).transpose(1, 2)
 
 
-@pytest.mark.parametrize("b,hq,hkv,t,lk,cap,kind", [
-    (4, 16, 8, 64, 3164, 3172, "lower_right"),  # the flow expert's step (4 episodes)
-    (2, 32, 8, 32, 1000, 1000, "lower_right"),  # 4 query heads per KV head, 128 rows
-    (3, 8, 8, 16, 100, 128, None),              # no mask, keys not a multiple of 64
-    (2, 16, 8, 64, 64, 64, "lower_right"),      # one block: plain causal
-    (2, 16, 8, 64, 700, 704, "random"),         # arbitrary mask, some rows see nothing
-    (2, 4, 2, 8, 200, 200, "per_head"),         # a mask per query head
+@pytest.mark.parametrize("b,hq,hkv,t,lk,cap,kind,d", [
+    (4, 16, 8, 64, 3164, 3172, "lower_right", 128),  # the flow expert's step (4 episodes)
+    (2, 32, 8, 32, 1000, 1000, "lower_right", 128),  # 4 query heads per KV head, 128 rows
+    (3, 8, 8, 16, 100, 128, None, 128),              # no mask, keys not a multiple of 64
+    (2, 16, 8, 64, 64, 64, "lower_right", 128),      # one block: plain causal
+    (2, 16, 8, 64, 700, 704, "random", 128),         # arbitrary mask, some rows see nothing
+    (2, 4, 2, 8, 200, 200, "per_head", 128),         # a mask per query head
+    (2, 16, 16, 1024, 1024, 1024, None, 80),         # the ViT: 128-patch tiles, head_dim 80
+    (1, 4, 4, 200, 300, 304, "random", 128),         # tiles with a ragged last one, masked
+    (1, 2, 2, 130, 77, 80, None, 96),                # ragged tiles and keys, head_dim 96
 ])
-def test_attention_rows(cuda, b, hq, hkv, t, lk, cap, kind):
+def test_attention_rows(cuda, b, hq, hkv, t, lk, cap, kind, d):
     from umic_b200.kernels.attention import attention_rows
 
-    d = 128
     q = _randn(b, t, hq, d, seed=90, dev=cuda).transpose(1, 2)  # HF's [B, Hq, T, D] view
     kbuf = _randn(b, hkv, cap, d, seed=91, dev=cuda)
     vbuf = _randn(b, hkv, cap, d, seed=92, dev=cuda)
@@ -504,7 +506,7 @@ def test_attention_rows(cuda, b, hq, hkv, t, lk, cap, kind):
         mask[..., 0] = True
     scale = d ** -0.5
     stats.clear()
-    out = attention_rows(q, k, v, mask, scale)
+    out = attention_rows(q, k, v, mask, scale)  # head dims below 128 are zero-padded inside
     assert out is not None and stats["umic_attention_rows"] == 1
     assert out.shape == (b, t, hq, d)
     ref = _attn_ref(q, k, v, mask, scale)
@@ -539,13 +541,13 @@ def test_mask_pack_bits(cuda, b, h, t, lk):
 def test_attention_rows_declines_uncovered_shapes(cuda):
     from umic_b200.kernels.attention import attention_rows
 
-    q = _randn(1, 16, 100, 128, seed=95, dev=cuda)  # 2 x 100 rows per KV head > 128
+    q = _randn(1, 16, 100, 128, seed=95, dev=cuda)  # 2 heads x 100 rows per KV head
     k = _randn(1, 8, 300, 128, seed=96, dev=cuda)
     stats.clear()
     assert attention_rows(q, k, k, None, 0.1) is None
-    q80 = _randn(1, 4, 8, 80, seed=97, dev=cuda)  # head_dim 80
-    k80 = _randn(1, 2, 64, 80, seed=98, dev=cuda)
-    assert attention_rows(q80, k80, k80, None, 0.1) is None
+    q48 = _randn(1, 4, 8, 48, seed=97, dev=cuda)  # head_dim 48
+    k48 = _randn(1, 2, 64, 48, seed=98, dev=cuda)
+    assert attention_rows(q48, k48, k48, None, 0.1) is None
     assert stats["attention_rows_fallback"] == 2 and stats["umic_attention_rows"] == 0
 
 

@@ -204,6 +204,7 @@ def test_vit_forward_vs_fp32(cuda, images):
         o_ours = vis(pix, grid_thw=grid)
     integrate.unfuse_mlps(holder)
     assert stats["umic_add_layernorm"] >= 27 and stats["umic_rope_inplace"] == 27
+    assert stats["umic_attention_rows"] == 27  # 1024-patch images: the tcgen05 attention
     assert stats["umic_gemm"] == 27 + 1  # fc1 + tanh-GELU per block, and the patch embed
     for name in ("pooler_output", "last_hidden_state"):
         a, b, c = getattr(o_ours, name), getattr(o_eager, name), getattr(o32, name)

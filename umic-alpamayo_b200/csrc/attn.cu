@@ -22,7 +22,10 @@
 //                           in log2 units (weights stay <= 256), i.e. rarely.
 // The two groups (warps 2-5 and 6-9, one of each on every SM sub-partition) run
 // independent chains on alternate blocks and exchange nothing until the end, where
-// each row's two partial results are merged with their maxima and sums. The MMA
+// each row's two partial results are merged with their maxima and sums. With one
+// query head per KV head, longer token ranges are cut into 128-row tiles, one CTA each
+// (the ViT: 1024 patches per image and head); head dims below 128 (the ViT's 80) are
+// zero-filled by TMA, which adds nothing to S or O. The MMA
 // for S of block j + 2 is issued as soon as group j % 2 has read S of block j, so
 // it runs while the group works on block j.
 //
@@ -78,6 +81,8 @@ struct AttnParams {
   int64_t o_sb, o_sh, o_st;
   uint32_t* err;
   int hq, hkv, g, t, lk, nblk;
+  int qtiles;  // > 1: one query head per KV head, rows t0 .. t0 + 127 per CTA (t0 = 128 qt)
+  int d;       // head dim (<= 128; the tiles are zero-filled past it)
   float scale_log2;         // softmax scale * log2(e)
 };
 
@@ -229,7 +234,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t s_empty0 = s_full + 16, p_full0 = s_full + 32, o_full0 = s_full + 64;
   const uint32_t o_last = s_full + 80, drain = s_full + 88;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x / p.hkv, h = blockIdx.x % p.hkv;
+  const int qt = static_cast<int>(blockIdx.x) % p.qtiles;
+  const int bh = static_cast<int>(blockIdx.x) / p.qtiles;
+  const int b = bh / p.hkv, h = bh % p.hkv;
+  const int t0 = qt * kRows;
   const uint32_t qs = sbase;
   auto kslot = [&](int s) { return sbase + kQBytes + s * kStageBytes; };
   auto vslot = [&](int s) { return sbase + kQBytes + s * kStageBytes + kKBytes; };
@@ -271,12 +279,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       bool ok = true;
-      // Q rows (g, t) -> tile row g * T + t; two 64-wide d halves (atom columns).
-      mbar_expect_tx(q_full, static_cast<uint32_t>(p.g * p.t) * kD * 2);
-      for (int g = 0; g < p.g; ++g)
+      // Q rows (g, t) -> tile row g * T + t (one tile), or t - t0 (tiled over tokens);
+      // two 64-wide d halves (atom columns); d past the head dim arrives as zeros.
+      if (p.qtiles == 1) {
+        mbar_expect_tx(q_full, static_cast<uint32_t>(p.g * p.t) * kD * 2);
+        for (int g = 0; g < p.g; ++g)
+          for (int half = 0; half < 2; ++half)
+            tma_load_4d(qs + half * (kQBytes / 2) + g * p.t * 128, &map_q, q_full, half * 64,
+                        h * p.g + g, 0, b);
+      } else {
+        mbar_expect_tx(q_full, kQBytes);
         for (int half = 0; half < 2; ++half)
-          tma_load_4d(qs + half * (kQBytes / 2) + g * p.t * 128, &map_q, q_full, half * 64,
-                      h * p.g + g, 0, b);
+          tma_load_4d(qs + half * (kQBytes / 2), &map_q, q_full, half * 64, h, t0, b);
+      }
       int j = 0;
       for (; j < p.nblk; ++j) {
         const int s = j % kStages;
@@ -395,8 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int grp = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
-    const bool valid = r < p.g * p.t;
-    const int g = valid ? r / p.t : 0, t = valid ? r % p.t : 0;
+    const bool tiled = p.qtiles > 1;
+    const bool valid = tiled ? t0 + r < p.t : r < p.g * p.t;
+    const int g = (!tiled && valid) ? r / p.t : 0;
+    const int t = tiled ? t0 + r : (valid ? r % p.t : 0);
     const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t ts = tmem_base + lanes + 64 * grp;
     const uint32_t to0 = tmem_base + lanes + kTmemO;  // O_0; O_1 is 128 columns on
@@ -542,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (valid) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
+            if (c + i >= p.d) break;  // columns past the head dim are padding
             float f[8];
 #pragma unroll
             for (int jj = 0; jj < 8; ++jj)
@@ -633,17 +651,23 @@ extern "C" int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, in
     return fail(UMIC_ERR_INVALID_ARG, "%s: bad sizes", kName);
   if (batch == 0 || t == 0) return UMIC_OK;
   if (!q || !k || !v || !out) return fail(UMIC_ERR_INVALID_ARG, "%s: null pointer", kName);
-  if (d != kD) return fail(UMIC_ERR_UNSUPPORTED, "%s: head_dim %lld (128 only)", kName,
-                           (long long)d);
+  if (d < 64 || d > kD || d % 8)
+    return fail(UMIC_ERR_UNSUPPORTED, "%s: head_dim %lld (64..128, a multiple of 8)", kName,
+                (long long)d);
   if (hq % hkv) return fail(UMIC_ERR_UNSUPPORTED, "%s: %lld query heads over %lld kv heads",
                             kName, (long long)hq, (long long)hkv);
   const int64_t g = hq / hkv;
   if (!(scale > 0.f)) return fail(UMIC_ERR_INVALID_ARG, "%s: scale must be positive", kName);
-  if (g * t > kRows || t % 8 || lk < 1)
+  // One tile of g * t <= 128 rows per KV head, or (one query head per KV head) tiles of
+  // 128 tokens.
+  const bool one_tile = g * t <= kRows && t % 8 == 0;
+  if ((!one_tile && g != 1) || lk < 1)
     return fail(UMIC_ERR_UNSUPPORTED,
-                "%s: %lld query rows per kv head (<= 128, tokens a multiple of 8, keys >= 1)",
+                "%s: %lld query rows per kv head (<= 128 with tokens a multiple of 8, or "
+                "one query head per kv head; keys >= 1)",
                 kName, (long long)(g * t));
-  if (batch * hkv > 0x7fffffffLL || lk > 0x7fffffffLL - kKeys)
+  const int64_t qtiles = one_tile ? 1 : (t + kRows - 1) / kRows;
+  if (batch * hkv * qtiles > 0x7fffffffLL || lk > 0x7fffffffLL - kKeys || t > 0x7fffffffLL)
     return fail(UMIC_ERR_UNSUPPORTED, "%s: size too large", kName);
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !stride_ok(q_sh) ||
       !stride_ok(q_st) || !stride_ok(q_sb) || !stride_ok(k_sl) || !stride_ok(k_sh) ||
@@ -654,9 +678,10 @@ extern "C" int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, in
     return fail(UMIC_ERR_INVALID_ARG, "%s: negative mask stride", kName);
   CUtensorMap mq, mk, mv;
   // q as (d, head, token, batch); k / v as (d, key, kv head, batch)
-  if (!make_map4(&mq, q, kD, hq, t, batch, q_sh, q_st, q_sb, 1, static_cast<int>(t)) ||
-      !make_map4(&mk, k, kD, lk, hkv, batch, k_sl, k_sh, k_sb, kKeys, 1) ||
-      !make_map4(&mv, v, kD, lk, hkv, batch, v_sl, v_sh, v_sb, kKeys, 1))
+  const int tbox = one_tile ? static_cast<int>(t) : kRows;
+  if (!make_map4(&mq, q, d, hq, t, batch, q_sh, q_st, q_sb, 1, tbox) ||
+      !make_map4(&mk, k, d, lk, hkv, batch, k_sl, k_sh, k_sb, kKeys, 1) ||
+      !make_map4(&mv, v, d, lk, hkv, batch, v_sl, v_sh, v_sb, kKeys, 1))
     return fail(UMIC_ERR_DEVICE, "%s: cuTensorMapEncodeTiled unavailable or rejected", kName);
   AttnParams p;
   p.bits = mask_bits;
@@ -674,6 +699,8 @@ extern "C" int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, in
   p.t = static_cast<int>(t);
   p.lk = static_cast<int>(lk);
   p.nblk = static_cast<int>((lk + kKeys - 1) / kKeys);
+  p.qtiles = static_cast<int>(qtiles);
+  p.d = static_cast<int>(d);
   p.scale_log2 = scale * 1.4426950408889634f;
   static std::once_flag once[64];
   int dev = 0;
@@ -685,7 +712,8 @@ extern "C" int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, in
   });
   if (e != cudaSuccess)
     return fail(UMIC_ERR_LAUNCH, "%s: smem attribute: %s", kName, cudaGetErrorString(e));
-  attn_rows_kernel<<<static_cast<unsigned>(batch * hkv), kThreads, kSmem, as_stream(stream)>>>(
+  attn_rows_kernel<<<static_cast<unsigned>(batch * hkv * qtiles), kThreads, kSmem,
+                     as_stream(stream)>>>(
       mq, mk, mv, p);
   return launch_status(kName);
 }

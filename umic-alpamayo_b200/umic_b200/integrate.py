@@ -513,8 +513,9 @@ def _fused_seqlen_attn_forward(self: nn.Module, hidden_states: torch.Tensor,
                                cu_seqlens: torch.Tensor, rotary_pos_emb=None,
                                position_embeddings=None, **kwargs) -> torch.Tensor:
     """One packed varlen attention call instead of split / per-image / cat
-    (src/umic/integrate.py:410-458). Attention itself stays a library kernel
-    (torch's flash attention); RoPE runs in place on the B200 kernel."""
+    (src/umic/integrate.py:410-458). Images of one size run on the tcgen05 attention
+    kernel; other packings keep torch's varlen flash attention. RoPE runs in place on
+    the B200 kernel."""
     import transformers.models.qwen3_vl.modeling_qwen3_vl as _mod
 
     seq_length = hidden_states.shape[0]
@@ -525,8 +526,23 @@ def _fused_seqlen_attn_forward(self: nn.Module, hidden_states: torch.Tensor,
     cache: dict = self._umic_attn_cache
     if cache.get("cu_seqlens_ref") is not cu_seqlens:
         cache["cu_seqlens_ref"] = cu_seqlens
-        cache["max_seqlen"] = int((cu_seqlens[1:] - cu_seqlens[:-1]).max().item())
+        lens = cu_seqlens[1:] - cu_seqlens[:-1]
+        lo, hi = (int(v) for v in torch.stack((lens.min(), lens.max())).tolist())
+        cache["max_seqlen"] = hi
+        cache["uniform_len"] = hi if lo == hi and hi > 0 else 0
     max_seqlen = cache["max_seqlen"]
+    n = cache["uniform_len"]
+    if n and query_states.is_cuda and query_states.dtype == torch.bfloat16:
+        # Images of one size: [images, heads, patches, head_dim] views of the packed
+        # qkv, attention on the tcgen05 kernel (128-patch tiles per image and head).
+        from .kernels.attention import attention_rows
+
+        imgs, heads, hd = seq_length // n, self.num_heads, query_states.shape[-1]
+        q4, k4, v4 = (t.view(imgs, n, heads, hd).transpose(1, 2)
+                      for t in (query_states, key_states, value_states))
+        out4 = attention_rows(q4, k4, v4, None, self.scaling)
+        if out4 is not None:
+            return self.proj(out4.reshape(seq_length, -1))
     out = torch.ops.aten._flash_attention_forward(
         query_states, key_states, value_states, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen,
         0.0, False, False, scale=self.scaling)
