@@ -171,16 +171,19 @@ UMIC_API int umic_qk_norm_rope_kv(
 
 /* out = softmax(scale * q . k^T, masked) . v with grouped-query heads, for few
  * query rows per KV head over a long key prefix (the flow expert's action tokens
- * over its cached prefix). q [batch, hq, t, 128] through strides (q_sb, q_sh,
- * q_st); k, v [batch, hkv, lk, 128] through (sb, sh, sl) -- e.g. the prefix view of
- * an in-place cache buffer; out [batch, hq, t, 128] through (o_sb, o_sh, o_st).
+ * over its cached prefix), or for one query head per KV head over 128-token tiles
+ * (the ViT's per-image attention). q [batch, hq, t, d] through strides (q_sb, q_sh,
+ * q_st); k, v [batch, hkv, lk, d] through (sb, sh, sl) -- e.g. the prefix view of
+ * an in-place cache buffer; out [batch, hq, t, d] through (o_sb, o_sh, o_st).
  * mask_bits: the mask as packed by umic_mask_pack_bits -- key k of (b, head, token)
  * attends iff bit k % 32 of word b*m_sb + head*m_sh + token*m_st + k / 32 is set (word
  * strides; 0 broadcasts) -- or NULL for no mask; rows that attend to nothing come
- * out as zeros. Covers head_dim 128, hq a multiple of hkv, (hq / hkv) * t <= 128 and
- * t a multiple of 8, 16-byte aligned bases and strides that are multiples of 8
- * elements; other shapes return UMIC_ERR_UNSUPPORTED / UMIC_ERR_ALIGNMENT and the
- * caller keeps its own attention. No kernel counterpart in the reference: it leaves
+ * out as zeros. Covers head_dim 64..128 (a multiple of 8), hq a multiple of hkv, and
+ * either (hq / hkv) * t <= 128 with t a multiple of 8 (one CTA per batch and kv head)
+ * or hq == hkv with any t (one CTA per 128 tokens, e.g. the ViT's 1024 patches per
+ * image), 16-byte aligned bases and strides that are multiples of 8 elements; other
+ * shapes return UMIC_ERR_UNSUPPORTED / UMIC_ERR_ALIGNMENT and the caller keeps its
+ * own attention. No kernel counterpart in the reference: it leaves
  * this attention to torch SDPA inside the HF attention forward that its flow-cache
  * hook serves (src/umic/integrate.py:715-756); this replaces that SDPA call. */
 UMIC_API int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,

@@ -7,7 +7,8 @@ q_norm / k_norm per head, apply_rotary_pos_emb, and the KV-cache write
 
 attention_rows: the attention itself for few query rows per KV head over a long
 cached prefix under a boolean mask -- the flow expert's action tokens over the
-prefix KV, which torch's SDPA sends to an sm80-generation cuDNN kernel.
+prefix KV, which torch's SDPA sends to an sm80-generation cuDNN kernel -- and for
+one query head per KV head in 128-token tiles (the ViT's per-image attention).
 """
 
 from __future__ import annotations
@@ -79,8 +80,9 @@ def attention_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     tensor broadcastable to [B, Hq, T, >= Lk] (True = attend) or None; the mask is
     packed to bits first (umic_mask_pack_bits, one launch). Returns
     [B, T, Hq, D] (the layout transformers' attention functions return), or None
-    when the kernel does not cover the shape (head_dim 128, Hq / Hkv * T <= 128
-    query rows per KV head, T a multiple of 8) so the caller keeps its own path.
+    when the kernel does not cover the shape (head_dim 64..128, a multiple of 8; either
+    Hq / Hkv * T <= 128 query rows per KV head with T a multiple of 8, or Hq == Hkv
+    with any T, cut into 128-token tiles) so the caller keeps its own path.
     """
     dev = require_cuda("attention_rows", q, k, v, mask)
     require_bf16("attention_rows", q, k, v)
