@@ -351,7 +351,8 @@ __global__ void __launch_bounds__(kStThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStStages * kStStageBytes);
-  // flags[0]: abort, flags[1]: "this CTA finishes the current row block"
+  // flags[0]: abort, flags[1]: "this CTA finishes the current row block", flags[2]: "the
+  // other contributor of the last row block has posted its partial"
   volatile int* flags = reinterpret_cast<volatile int*>(bars + 2 * kStStages);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStStages);
   const uint32_t sbase = smem_u32(smem);
@@ -366,6 +367,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
     }
     flags[0] = 0;
     flags[1] = 0;
+    flags[2] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&m0);
     if (kGated || a.nseg > 1) prefetch_map(&m1);
@@ -446,6 +448,44 @@ __global__ void __launch_bounds__(kStThreads, 1)
   // x, y and the workspace may still belong to the previous kernel in the stream.
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
+  // The last row block of this CTA's range, when it has exactly one other contributor
+  // and that one has already posted its partial: its partial is fetched while this CTA
+  // streams its own last units (oth), and the block is summed and written without the
+  // count round trip. fast == false keeps the general path below.
+  constexpr int kVals = MC * 4 * (kGated ? 2 : 1);
+  const int rb_last = u1 > u0 ? (u1 - 1) / a.nkc : -1;
+  bool fast = false;
+  bool fast_first = false;  // this CTA is the block's first contributor
+  float oth[kVals];
+  // slot 0 holds a CTA's first row block, slot 1 its last one
+  auto slot_for = [&](int cta, int rb) {
+    const int side = (rb == st_unit_begin(cta, a) / a.nkc) ? 0 : 1;
+    return a.slots + (static_cast<size_t>(cta) * 2 + side) * 2 * kStPlane;
+  };
+  auto try_fast = [&](int rb) {
+    const int first = st_cta_of(rb * a.nkc, a), last = st_cta_of((rb + 1) * a.nkc - 1, a);
+    if (last - first != 1) return;
+    if (warp == 0 && lane == 0) {
+      // acquire: pairs with the other contributor's release of the count
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.cnt + rb) : "memory");
+      flags[2] = v == 1u;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kStConsumers * 32) : "memory");
+    if (!flags[2]) return;
+    fast = true;
+    fast_first = first == c;
+    const float* src = slot_for(fast_first ? last : first, rb);
+#pragma unroll
+    for (int mc = 0; mc < MC; ++mc)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int rr = j < 2 ? r0 : r1, mcol = mc * 8 + 2 * t + (j & 1);
+        oth[mc * 4 + j] = __ldcg(src + rr * 16 + mcol);
+        if constexpr (kGated) oth[MC * 4 + mc * 4 + j] = __ldcg(src + kStPlane + rr * 16 + mcol);
+      }
+  };
+
   // Writes row block rb: directly when this CTA holds all of it, else via the slots.
   auto flush = [&](int rb) {
     const int first = st_cta_of(rb * a.nkc, a), last = st_cta_of((rb + 1) * a.nkc - 1, a);
@@ -474,11 +514,27 @@ __global__ void __launch_bounds__(kStThreads, 1)
           emit(j < 2 ? r0 : r1, mc * 8 + 2 * t + (j & 1), acc[mc][j], kGated ? acc2[mc][j] : 0.f);
       return;
     }
-    // slot 0 holds a CTA's first row block, slot 1 its last one
-    auto slot_of = [&](int cta) {
-      const int side = (rb == st_unit_begin(cta, a) / a.nkc) ? 0 : 1;
-      return a.slots + (static_cast<size_t>(cta) * 2 + side) * 2 * kStPlane;
-    };
+    if (fast && rb == rb_last) {
+      // the same sums, in the same CTA order, as the general path below
+#pragma unroll
+      for (int mc = 0; mc < MC; ++mc)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float o1 = oth[mc * 4 + j], o2 = kGated ? oth[MC * 4 + mc * 4 + j] : 0.f;
+          const float m1 = acc[mc][j], m2 = kGated ? acc2[mc][j] : 0.f;
+          float v = 0.f, v2 = 0.f;
+          v += fast_first ? m1 : o1;
+          v += fast_first ? o1 : m1;
+          if constexpr (kGated) {
+            v2 += fast_first ? m2 : o2;
+            v2 += fast_first ? o2 : m2;
+          }
+          emit(j < 2 ? r0 : r1, mc * 8 + 2 * t + (j & 1), v, v2);
+        }
+      if (warp == 0 && lane == 0) a.cnt[rb] = 0;  // both contributors are done with it
+      return;
+    }
+    auto slot_of = [&](int cta) { return slot_for(cta, rb); };
     float* mine = slot_of(c);
 #pragma unroll
     for (int mc = 0; mc < MC; ++mc)
@@ -502,7 +558,6 @@ __global__ void __launch_bounds__(kStThreads, 1)
     asm volatile("bar.sync 1, %0;" ::"n"(kStConsumers * 32) : "memory");
     if (!flags[1]) return;
     // All partial loads in flight at once, then sums in CTA order.
-    constexpr int kVals = MC * 4 * (kGated ? 2 : 1);
     float part[kStMaxContrib][kVals];
 #pragma unroll
     for (int q = 0; q < kStMaxContrib; ++q) {
@@ -550,6 +605,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
         zero_acc();
       }
       cur = rb;
+      if (rb == rb_last) try_fast(rb);
     }
     // this chunk's activations, requested before the weights land
     uint4 xv[kSlabs][MC];
