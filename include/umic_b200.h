@@ -92,6 +92,19 @@ UMIC_API int umic_add_rmsnorm(const void* x, int64_t x_row_stride, const void* r
                      int64_t normed_row_stride, void* summed, int64_t summed_row_stride,
                      int64_t rows, int64_t n, float eps, void* stream);
 
+/* y = bf16(base + alpha * (x * rsqrt(mean(x^2) + eps) * w)), fp32 inside, one
+ * rounding: RMSNorm with an axpy epilogue. The flow sampler's Euler update
+ * x <- x + dt * v, where the velocity v is the action expert's final RMSNorm output,
+ * runs as this one pass (v is never stored). y may be base itself (same pointer and
+ * row stride); row strides must be positive.
+ * Replaces the expert's final norm (_patched_rmsnorm_forward, integrate.py:134-141)
+ * together with P9 ode_step, x <- x + dt*v (docs/260610_01_umic_design_ko.md:72),
+ * which the reference lists but never builds. */
+UMIC_API int umic_rmsnorm_axpy(const void* x, int64_t x_row_stride, const void* w, int w_dtype,
+                               const void* base, int64_t base_row_stride, float alpha, void* y,
+                               int64_t y_row_stride, int64_t rows, int64_t n, float eps,
+                               void* stream);
+
 /* ---- LayerNorm family (src/umic/kernels/layernorm.py) -------------------- */
 
 /* y = bf16((x - mean) * rsqrt(var + eps) * w + b), fp32 inside; w and b share

@@ -23,6 +23,7 @@ from .formulas import (  # noqa: F401
     rel_err,
     max_rel_err,
     rmsnorm,
+    rmsnorm_axpy,
     rope_rotate_half,
     swiglu_block,
     text_rope_cos_sin,

@@ -40,6 +40,13 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return xf * torch.rsqrt(var + eps) * _f(w)
 
 
+def rmsnorm_axpy(x, w, eps, base, alpha):
+    """base + alpha * rmsnorm(x) in fp32: the flow sampler's Euler step x + dt * v with
+    v the expert's final RMSNorm output (P9 ode_step, docs/260610_01_umic_design_ko.md:72,
+    composed with rmsnorm.py:44-51)."""
+    return _f(base) + float(alpha) * rmsnorm(x, w, eps)
+
+
 def add_rmsnorm(x, r, w, eps):
     """(normed, summed): s = x + r in fp32, normed = rmsnorm(s) (rmsnorm.py:91-101)."""
     s = _f(x) + _f(r)

@@ -46,3 +46,21 @@ def gloo_rank(rank, world, port, out):
         out.put((rank, m, gathered))
     finally:
         dist.destroy_process_group()
+
+
+def bench_ranks(rank, world, port, out):
+    """bench.py's host coordination on gloo: its cfg4 / cfg5 episode shards, barrier
+    and max over ranks, as each torchrun rank runs them."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    import bench
+
+    ranks = bench.Ranks(world)
+    try:
+        lm = bench._share(bench.TOTAL_EPISODES, rank, world)
+        flow = bench._share(bench.FLOW_EPISODES, rank, world)
+        ranks.barrier()
+        m = ranks.max(float(flow[1] * 10 + rank))
+        out.put((rank, lm, flow, m))
+    finally:
+        ranks.close()

@@ -72,7 +72,7 @@ def test_views_not_copies(fake_kernel):
     dyn, _ = _dyn()
     c = InplaceKVCache.from_dynamic(dyn, extra_tokens=4)
     k, _ = c.layers[0].update(torch.ones(2, 3, 1, 8), torch.ones(2, 3, 1, 8))
-    assert k.data_ptr() == c.layers[0]._k_buf.data_ptr()  # a prefix view of the buffer
+    assert k.data_ptr() == c.layers[0].k_buf.data_ptr()  # a prefix view of the buffer
 
 
 def test_graph_mode_writes_at_device_position(fake_kernel):

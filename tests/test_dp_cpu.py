@@ -1,6 +1,7 @@
 """Episode data parallelism on CPU: sharding, the process launcher with injected
 failures (an exception, a non-zero exit, a hang), and the world-size-2 gloo path
-bench.py uses for its barrier and max-over-ranks timing."""
+bench.py uses for its barrier and max-over-ranks timing (with bench.py's own
+cfg4 / cfg5 sharding)."""
 
 import multiprocessing as mp
 import socket
@@ -71,3 +72,29 @@ def test_gloo_world_size_2_barrier_and_max():
     # rank 0: episodes 0..3 (sum 6); rank 1: 4..7 (sum 22) + 1 -> max 23 on both
     assert out[0][1] == out[1][1] == 23.0
     assert out[0][2] == [[0, 1, 2, 3], [4, 5, 6, 7]]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_bench_gloo_ranks_shard_cfg4_and_cfg5(world):
+    """bench.py's Ranks on a gloo group: every cfg4 (8) and cfg5 (32) episode lands on
+    exactly one rank in contiguous blocks, and the max over ranks reaches every rank."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=dp_workers.bench_ranks, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=180) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for total, col in ((8, 1), (32, 2)):
+        covered = []
+        for row in out:
+            first, count = row[col]
+            covered.extend(range(first, first + count))
+        assert covered == list(range(total))
+    flow_counts = [row[2][1] for row in out]
+    expect = max(c * 10 + r for r, c in enumerate(flow_counts))
+    assert all(row[3] == expect for row in out)

@@ -13,7 +13,7 @@ import oracle
 from umic_b200 import _lib
 from umic_b200.kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inplace,
                                apply_rotary_vision, gate_silu_mul, gate_silu_mul_nk, kv_append,
-                               layernorm, linear, linear_gemv, rmsnorm, stats)
+                               layernorm, linear, linear_gemv, rmsnorm, rmsnorm_axpy, stats)
 from umic_b200.kernels.attention import qk_norm_rope_kv
 from umic_b200.kernels.linear import linear_gemv_multi
 
@@ -62,6 +62,36 @@ def test_add_rmsnorm(cuda, rows, n):
     rn, rs = oracle.add_rmsnorm(x.cpu(), r.cpu(), w.cpu(), 1e-6)
     _close(normed, rn)
     _close(summed, rs)
+
+
+@pytest.mark.parametrize("rows,n", [(32 * 64, 2048), (99, 128), (5, 2048), (3, 100), (1, 8)])
+@pytest.mark.parametrize("inplace", [False, True])
+def test_rmsnorm_axpy(cuda, rows, n, inplace):
+    """The flow sampler's Euler update x + dt * rmsnorm(h) * w in one pass (cfg5 shape:
+    32 episodes x 64 action tokens x 2048), against the fp32 formula; in place
+    (out = x) and out of place; (3, 100) takes the unaligned scalar path."""
+    h = _randn(rows, n, seed=40, dev=cuda)
+    x = _randn(rows, n, seed=41, dev=cuda)
+    w = (1 + 0.05 * _randn(n, seed=42, dev="cpu", dtype=torch.float32)).to(torch.bfloat16)
+    w = w.to(cuda)
+    ref = oracle.rmsnorm_axpy(h.cpu(), w.cpu(), 1e-6, x.cpu(), 0.1)
+    if inplace:
+        y = rmsnorm_axpy(h, w, 1e-6, x, 0.1, out=x)
+        assert y is x
+    else:
+        x0 = x.clone()
+        y = rmsnorm_axpy(h, w, 1e-6, x, 0.1)
+        assert torch.equal(x, x0)
+    _close(y, ref)
+
+
+def test_rmsnorm_axpy_strided_rows(cuda):
+    big = _randn(64, 2048 + 64, seed=43, dev=cuda)
+    h = big[:, :2048]  # row stride 2112
+    x = _randn(64, 2048, seed=44, dev=cuda)
+    w = _randn(2048, seed=45, dev=cuda)
+    _close(rmsnorm_axpy(h, w, 1e-6, x, -0.25), oracle.rmsnorm_axpy(h.cpu(), w.cpu(), 1e-6,
+                                                                  x.cpu(), -0.25))
 
 
 def test_rmsnorm_strided_rows(cuda):

@@ -73,10 +73,11 @@ def test_apply_report_and_patching():
         assert report["ve_layernorm_fused"] == 11 and report["ve_pipeline_fused"] == 1
         assert report["ve_patch_embed_fused"] == 1 and report["ve_attn_varlen_fused"] == 4
         lm = model.vlm.model.language_model
-        assert lm.layers[0].mlp.forward.__func__ is integrate._fused_mlp_forward
-        assert lm.layers[0].self_attn.q_proj.forward.__func__ is integrate._patched_linear_forward
-        assert lm.layers[0].input_layernorm.forward.__func__ is \
-            integrate._patched_rmsnorm_forward
+        assert lm.layers[0].mlp.forward.__func__ is integrate._swiglu_forward
+        assert lm.layers[0].self_attn.q_proj.forward.__func__ is integrate._projection_forward
+        assert lm.layers[0].input_layernorm.forward.__func__ is integrate._rmsnorm_forward
+        assert isinstance(lm.layers[0].mlp._umic_site, integrate.SwiGLUSite)
+        assert lm.layers[0].mlp._umic_site.gate is lm.layers[0].mlp.gate_proj
         import transformers.models.qwen3_vl.modeling_qwen3_vl as mod
         assert getattr(mod.apply_rotary_pos_emb, "_umic_fused", False)
         # weights shared, never copied
@@ -85,6 +86,8 @@ def test_apply_report_and_patching():
     finally:
         integrate.unfuse_rope()
         integrate.unfuse_mlps(model)
+    assert not any("forward" in m.__dict__ or "_umic_site" in m.__dict__
+                   for m in model.modules())
 
 
 def test_nothing_matches_is_a_noop():

@@ -11,6 +11,11 @@
 // several warps. Statistics and the scaled output are computed in fp32 and
 // rounded to bf16 once, as in the reference kernels (rmsnorm.py:44-51,91-101;
 // layernorm.py:43-52,87-100).
+//
+// The RMSNorm variant with an axpy epilogue (umic_rmsnorm_axpy) writes
+// y = base + alpha * normed instead of normed: the flow sampler's Euler update
+// x <- x + dt * v, where the velocity v is the expert's final RMSNorm output,
+// costs no extra pass over HBM (base read once, y written once, v never stored).
 #include "common.cuh"
 
 namespace umic {
@@ -25,7 +30,9 @@ struct NormArgs {
   const void* b;  // LayerNorm bias
   __nv_bfloat16* y;  // normed output
   __nv_bfloat16* s;  // summed output, add variants only
-  int64_t sx, sr, sy, ss;
+  const __nv_bfloat16* base;  // axpy epilogue: y = base + alpha * normed
+  int64_t sx, sr, sy, ss, sb;
+  float alpha;
   int64_t rows;
   int n;
   int w_dtype;
@@ -54,7 +61,7 @@ __device__ __forceinline__ float group_sum(float v, float* red) {
   return v;
 }
 
-template <int TPR, int VPT, bool kAdd, bool kLayerNorm>
+template <int TPR, int VPT, bool kAdd, bool kLayerNorm, bool kAxpy = false>
 __global__ void __launch_bounds__(kThreads) norm_vec_kernel(NormArgs a) {
   allow_dependent_launch();
   constexpr int kRowsPerCta = kThreads / TPR;
@@ -128,6 +135,12 @@ __global__ void __launch_bounds__(kThreads) norm_vec_kernel(NormArgs a) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rstd * w[j];
     }
+    if constexpr (kAxpy) {
+      float xb[8];
+      unpack8(ld_stream(a.base + row * a.sb + c * 8), xb);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = fmaf(a.alpha, o[j], xb[j]);
+    }
     st_vec(a.y + row * a.sy + c * 8, pack8(o));
   }
 }
@@ -136,7 +149,7 @@ __global__ void __launch_bounds__(kThreads) norm_vec_kernel(NormArgs a) {
 // (after the residual add) staged in shared memory so x / r are read once.
 constexpr int kScalarMaxN = 16384;
 
-template <bool kAdd, bool kLayerNorm>
+template <bool kAdd, bool kLayerNorm, bool kAxpy = false>
 __global__ void __launch_bounds__(kThreads) norm_scalar_kernel(NormArgs a) {
   allow_dependent_launch();
   extern __shared__ float srow[];
@@ -171,34 +184,36 @@ __global__ void __launch_bounds__(kThreads) norm_scalar_kernel(NormArgs a) {
     float o;
     if constexpr (kLayerNorm) o = (srow[j] - mean) * rstd * w + load_w1(a.b, a.w_dtype, j);
     else o = srow[j] * rstd * w;
+    if constexpr (kAxpy) o = fmaf(a.alpha, o, bf(a.base[row * a.sb + j]));
     a.y[row * a.sy + j] = __float2bfloat16_rn(o);
   }
 }
 
-template <int TPR, int VPT, bool kAdd, bool kLN>
+template <int TPR, int VPT, bool kAdd, bool kLN, bool kAxpy>
 void launch_vec(const NormArgs& a, cudaStream_t st) {
   constexpr int kRowsPerCta = kThreads / TPR;
   const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
-  prefer_max_shared<norm_vec_kernel<TPR, VPT, kAdd, kLN>>();
-  norm_vec_kernel<TPR, VPT, kAdd, kLN><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(a);
+  prefer_max_shared<norm_vec_kernel<TPR, VPT, kAdd, kLN, kAxpy>>();
+  norm_vec_kernel<TPR, VPT, kAdd, kLN, kAxpy>
+      <<<static_cast<unsigned>(grid), kThreads, 0, st>>>(a);
 }
 
-template <bool kAdd, bool kLN>
+template <bool kAdd, bool kLN, bool kAxpy = false>
 int dispatch(const NormArgs& a, bool vec_ok, cudaStream_t st) {
   if (a.rows > 0x7fffffffLL) return fail(UMIC_ERR_UNSUPPORTED, "norm: too many rows");
   const int c = a.n >> 3;
   if (vec_ok) {
-    if (c <= 4) launch_vec<4, 1, kAdd, kLN>(a, st);
-    else if (c <= 8) launch_vec<8, 1, kAdd, kLN>(a, st);
-    else if (c <= 16) launch_vec<16, 1, kAdd, kLN>(a, st);
-    else if (c <= 32) launch_vec<32, 1, kAdd, kLN>(a, st);
-    else if (c <= 64) launch_vec<32, 2, kAdd, kLN>(a, st);
-    else if (c <= 128) launch_vec<32, 4, kAdd, kLN>(a, st);
-    else if (c <= 160) launch_vec<32, 5, kAdd, kLN>(a, st);
-    else if (c <= 256) launch_vec<64, 4, kAdd, kLN>(a, st);
-    else if (c <= 512) launch_vec<128, 4, kAdd, kLN>(a, st);
-    else if (c <= 1024) launch_vec<256, 4, kAdd, kLN>(a, st);
-    else if (c <= 2048) launch_vec<256, 8, kAdd, kLN>(a, st);
+    if (c <= 4) launch_vec<4, 1, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 8) launch_vec<8, 1, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 16) launch_vec<16, 1, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 32) launch_vec<32, 1, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 64) launch_vec<32, 2, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 128) launch_vec<32, 4, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 160) launch_vec<32, 5, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 256) launch_vec<64, 4, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 512) launch_vec<128, 4, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 1024) launch_vec<256, 4, kAdd, kLN, kAxpy>(a, st);
+    else if (c <= 2048) launch_vec<256, 8, kAdd, kLN, kAxpy>(a, st);
     else vec_ok = false;
   }
   if (!vec_ok) {
@@ -206,10 +221,11 @@ int dispatch(const NormArgs& a, bool vec_ok, cudaStream_t st) {
       return fail(UMIC_ERR_UNSUPPORTED, "norm: n=%d exceeds %d", a.n, kScalarMaxN);
     const size_t smem = static_cast<size_t>(a.n) * sizeof(float);
     if (smem > 48 * 1024)
-      cudaFuncSetAttribute(norm_scalar_kernel<kAdd, kLN>,
+      cudaFuncSetAttribute(norm_scalar_kernel<kAdd, kLN, kAxpy>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    prefer_max_shared<norm_scalar_kernel<kAdd, kLN>>();
-    norm_scalar_kernel<kAdd, kLN><<<static_cast<unsigned>(a.rows), kThreads, smem, st>>>(a);
+    prefer_max_shared<norm_scalar_kernel<kAdd, kLN, kAxpy>>();
+    norm_scalar_kernel<kAdd, kLN, kAxpy>
+        <<<static_cast<unsigned>(a.rows), kThreads, smem, st>>>(a);
   }
   return launch_status("norm launch");
 }
@@ -252,7 +268,7 @@ int umic_rmsnorm(const void* x, int64_t sx, const void* w, int w_dtype, void* y,
   if (int rc = check_common("umic_rmsnorm", x, w, y, rows, n, w_dtype)) return rc;
   if (rows == 0) return UMIC_OK;
   NormArgs a{static_cast<const __nv_bfloat16*>(x), nullptr, w, nullptr,
-             static_cast<__nv_bfloat16*>(y), nullptr, sx, 0, sy, 0, rows,
+             static_cast<__nv_bfloat16*>(y), nullptr, nullptr, sx, 0, sy, 0, 0, 0.f, rows,
              static_cast<int>(n), w_dtype, eps};
   return dispatch<false, false>(a, vec_ok(n, {x, y}, {sx, sy}, w, w_dtype), as_stream(stream));
 }
@@ -266,7 +282,7 @@ int umic_add_rmsnorm(const void* x, int64_t sx, const void* r, int64_t sr, const
   if (!r || !summed) return fail(UMIC_ERR_INVALID_ARG, "umic_add_rmsnorm: null pointer");
   NormArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(r), w,
              nullptr, static_cast<__nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(summed),
-             sx, sr, sn, ss, rows, static_cast<int>(n), w_dtype, eps};
+             nullptr, sx, sr, sn, ss, 0, 0.f, rows, static_cast<int>(n), w_dtype, eps};
   return dispatch<true, false>(
       a, vec_ok(n, {x, r, normed, summed}, {sx, sr, sn, ss}, w, w_dtype), as_stream(stream));
 }
@@ -278,7 +294,7 @@ int umic_layernorm(const void* x, int64_t sx, const void* w, const void* b, int 
   if (rows == 0) return UMIC_OK;
   if (!b) return fail(UMIC_ERR_INVALID_ARG, "umic_layernorm: null bias");
   NormArgs a{static_cast<const __nv_bfloat16*>(x), nullptr, w, b,
-             static_cast<__nv_bfloat16*>(y), nullptr, sx, 0, sy, 0, rows,
+             static_cast<__nv_bfloat16*>(y), nullptr, nullptr, sx, 0, sy, 0, 0, 0.f, rows,
              static_cast<int>(n), w_dtype, eps};
   bool ok = vec_ok(n, {x, y}, {sx, sy}, w, w_dtype) && vec_ok(n, {}, {}, b, w_dtype);
   return dispatch<false, true>(a, ok, as_stream(stream));
@@ -292,11 +308,27 @@ int umic_add_layernorm(const void* x, int64_t sx, const void* r, int64_t sr, con
   if (rows == 0) return UMIC_OK;
   if (!r || !summed || !b) return fail(UMIC_ERR_INVALID_ARG, "umic_add_layernorm: null pointer");
   NormArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(r), w, b,
-             static_cast<__nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(summed), sx, sr,
-             sn, ss, rows, static_cast<int>(n), w_dtype, eps};
+             static_cast<__nv_bfloat16*>(normed), static_cast<__nv_bfloat16*>(summed), nullptr,
+             sx, sr, sn, ss, 0, 0.f, rows, static_cast<int>(n), w_dtype, eps};
   bool ok = vec_ok(n, {x, r, normed, summed}, {sx, sr, sn, ss}, w, w_dtype) &&
             vec_ok(n, {}, {}, b, w_dtype);
   return dispatch<true, true>(a, ok, as_stream(stream));
+}
+
+int umic_rmsnorm_axpy(const void* x, int64_t sx, const void* w, int w_dtype, const void* base,
+                      int64_t sb, float alpha, void* y, int64_t sy, int64_t rows, int64_t n,
+                      float eps, void* stream) {
+  clear_error();
+  if (int rc = check_common("umic_rmsnorm_axpy", x, w, y, rows, n, w_dtype)) return rc;
+  if (rows == 0) return UMIC_OK;
+  if (!base) return fail(UMIC_ERR_INVALID_ARG, "umic_rmsnorm_axpy: null base");
+  if (sx <= 0 || sb <= 0 || sy <= 0)
+    return fail(UMIC_ERR_INVALID_ARG, "umic_rmsnorm_axpy: row strides must be positive");
+  NormArgs a{static_cast<const __nv_bfloat16*>(x), nullptr, w, nullptr,
+             static_cast<__nv_bfloat16*>(y), nullptr, static_cast<const __nv_bfloat16*>(base),
+             sx, 0, sy, 0, sb, alpha, rows, static_cast<int>(n), w_dtype, eps};
+  return dispatch<false, false, true>(a, vec_ok(n, {x, y, base}, {sx, sy, sb}, w, w_dtype),
+                                      as_stream(stream));
 }
 
 }  // extern "C"

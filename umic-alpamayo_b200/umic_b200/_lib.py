@@ -32,6 +32,8 @@ _SIGNATURES: dict[str, list] = {
     "umic_set_device": [_c_int],
     "umic_device_errors": [ctypes.POINTER(ctypes.c_uint32), _c_int],
     "umic_rmsnorm": [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_i64, _c_f32, _c_p],
+    "umic_rmsnorm_axpy": [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_f32, _c_p, _c_i64,
+                          _c_i64, _c_i64, _c_f32, _c_p],
     "umic_add_rmsnorm": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_p, _c_i64,
                          _c_i64, _c_i64, _c_f32, _c_p],
     "umic_layernorm": [_c_p, _c_i64, _c_p, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_i64, _c_f32,

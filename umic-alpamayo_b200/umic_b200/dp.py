@@ -4,7 +4,7 @@ Inference episodes are independent, so they are split into contiguous blocks,
 one per rank, and each rank runs its block on its own GPU. Nothing is
 exchanged on the data path (no NCCL); the only cross-rank operations are the
 start barrier and the max-over-ranks of the timing, which bench.py takes from
-torch.distributed (`max_over_ranks` below).
+a torch.distributed gloo group (`max_over_ranks` below; CPU tensors, no NCCL).
 
 `run_workers` is the host-side launcher for jobs that do not come from
 torchrun: it spawns one process per rank (CUDA_VISIBLE_DEVICES pinned when GPUs

@@ -5,6 +5,8 @@
 * vision (cfg3): the 27-block ViT over 16 images of 448 x 448 (16 384 patches),
   unpatched transformers eager vs after `apply()` (fused pipeline: patch-embed GEMM,
   add+LayerNorm, in-place vision RoPE, packed varlen attention, fc1 + tanh-GELU GEMM).
+* kernels (cfg1, cfg2): the SwiGLU block and the four norm / RoPE kernels at the
+  BASELINE sizes against the unfused torch-eager GPU path, after an L2 flush.
 * flow (cfg5): the 18-layer action expert, 32 episodes x 64 action tokens over a
   3100-token prefix KV, 10 Euler steps; unpatched eager vs after `apply()`, with the
   Euler step run eagerly and as a replayed CUDA graph.
@@ -19,6 +21,7 @@ from __future__ import annotations
 
 import json
 import statistics
+import types
 
 import torch
 
@@ -59,6 +62,7 @@ def measure_vision(dev: torch.device, images: int = 16) -> dict:
 
     eager_ms = _timed(run)
     ref = run().last_hidden_state
+    ref32 = _fp32_vision(vis, pix, grid)
     holder = torch.nn.Module()
     holder.vlm = torch.nn.Module()
     holder.vlm.visual = vis
@@ -72,7 +76,142 @@ def measure_vision(dev: torch.device, images: int = 16) -> dict:
     return {"images": images, "patches": int(pix.shape[0]), "eager_ms": eager_ms,
             "ms": ours_ms, "speedup": eager_ms / ours_ms,
             "rel_err_vs_eager": _rel(got, ref),
+            "rel_err_vs_fp32": {"ours": _rel(got, ref32), "eager": _rel(ref, ref32)},
             "fused": {k: v for k, v in report.items() if k.startswith("ve_")}}
+
+
+class FlushTimer:
+    """CUDA-event time of one call after an L2 flush (a 256 MB write: L2 is 126 MB), so
+    an HBM-bound kernel whose inputs fit in L2 is still timed from HBM."""
+
+    def __init__(self, dev: torch.device):
+        self.scratch = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def __call__(self, fn, runs: int = 20, warmup: int = 3) -> float:
+        for _ in range(warmup):
+            fn()
+        out = []
+        for _ in range(runs):
+            self.scratch.zero_()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            out.append(s.elapsed_time(e))
+        return statistics.median(out)
+
+
+def measure_kernels(dev: torch.device, peaks: dict | None = None) -> dict:
+    """cfg1 (the pre-norm SwiGLU block) and cfg2 a-d (add+RMSNorm, add+LayerNorm, text
+    and vision RoPE in place) on the fused kernels vs the unfused torch-eager GPU path
+    (HF modules / functions), BASELINE sizes and seeds; each after an L2 flush. Achieved
+    rates are algorithmic bytes (each tensor read / written once) or FLOPs per call."""
+    import transformers.models.qwen3_vl.modeling_qwen3_vl as hf
+
+    from .kernels import add_layernorm, add_rmsnorm, apply_rotary_vision
+    from .kernels.rope import apply_rotary_text_inplace
+
+    peaks = peaks or {}
+    hbm = peaks.get("hbm_gbs")
+    tc = peaks.get("bf16_tflops")
+    timer = FlushTimer(dev)
+    F = torch.nn.functional
+    out: dict = {}
+
+    def gen(seed):
+        return torch.Generator(device="cpu").manual_seed(seed)
+
+    def rn(g, *shape, scale=1.0):
+        return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).to(dev)
+
+    # ---- cfg1: out = (x + r) + down(silu(gate(n)) * up(n)), n = RMSNorm(x + r)
+    g = gen(0)
+    m, h, i = 3100, 4096, 12288
+    x, r = rn(g, m, h), rn(g, m, h)
+    w = (1 + 0.05 * torch.randn(h, generator=g)).to(torch.bfloat16).to(dev)
+    wg, wu, wd = rn(g, i, h, scale=0.02), rn(g, i, h, scale=0.02), rn(g, h, i, scale=0.02)
+    mlp = types.SimpleNamespace(gate_proj=types.SimpleNamespace(weight=wg, bias=None),
+                                up_proj=types.SimpleNamespace(weight=wu, bias=None),
+                                down_proj=types.SimpleNamespace(weight=wd, bias=None))
+    norm = hf.Qwen3VLTextRMSNorm(h, eps=1e-6).to(device=dev, dtype=torch.bfloat16)
+    norm.weight.data.copy_(w)
+
+    def fused_block():
+        n, s = add_rmsnorm(x, r, w, 1e-6)
+        return integrate.mlp_forward(mlp, n, residual=s)
+
+    def eager_block():
+        s = x + r
+        n = norm(s)
+        return s + F.linear(F.silu(F.linear(n, wg)) * F.linear(n, wu), wd)
+
+    flops = 2.0 * m * h * i * 3
+    with torch.no_grad():
+        ms, ms_e = timer(fused_block, runs=10), timer(eager_block, runs=10)
+    out["cfg1_swiglu_block"] = {"ms": ms, "eager_ms": ms_e, "tflops": flops / ms / 1e9,
+                                "frac_of_burst_peak": flops / ms / 1e9 / tc if tc else None}
+    del x, r, wg, wu, wd, mlp
+
+    def hbm_entry(name, ours, eager, nbytes):
+        with torch.no_grad():
+            us, us_e = timer(ours) * 1e3, timer(eager) * 1e3
+        out[name] = {"us": us, "eager_us": us_e, "gbs": nbytes / us / 1e3,
+                     "frac_of_hbm": nbytes / us / 1e3 / hbm if hbm else None}
+
+    # ---- cfg2 (seed 1): (a) add+RMSNorm [3100, 4096]
+    g = gen(1)
+    xa, ra = rn(g, 3100, 4096), rn(g, 3100, 4096)
+    wa = torch.ones(4096, device=dev, dtype=torch.bfloat16)
+    hbm_entry("cfg2a_add_rmsnorm", lambda: add_rmsnorm(xa, ra, wa, 1e-6),
+              lambda: (norm(xa + ra)), 4 * 3100 * 4096 * 2)
+    # (b) add+LayerNorm [16384, 1280]
+    xb, rb = rn(g, 16384, 1280), rn(g, 16384, 1280)
+    ln = torch.nn.LayerNorm(1280, eps=1e-6).to(device=dev, dtype=torch.bfloat16)
+    hbm_entry("cfg2b_add_layernorm",
+              lambda: add_layernorm(xb, rb, ln.weight, ln.bias, 1e-6),
+              lambda: ln(xb + rb), 4 * 16384 * 1280 * 2)
+    # (c) text RoPE theta 1e6, q [1, 32, 3100, 128], k [1, 8, 3100, 128] (HF layouts)
+    from .workloads import text_config
+
+    rot = hf.Qwen3VLTextRotaryEmbedding(text_config()).to(dev)
+    qc, kc = rn(g, 1, 3100, 32, 128).transpose(1, 2), rn(g, 1, 3100, 8, 128).transpose(1, 2)
+    pos = torch.arange(3100, device=dev)[None].expand(3, 1, 3100)
+    cos, sin = rot(qc, pos)
+    orig_text = getattr(hf.apply_rotary_pos_emb, "_umic_original", hf.apply_rotary_pos_emb)
+    hbm_entry("cfg2c_text_rope", lambda: apply_rotary_text_inplace(qc, kc, cos, sin),
+              lambda: orig_text(qc, kc, cos, sin),
+              2 * (32 + 8) * 3100 * 128 * 2 + 2 * 3100 * 128 * 2)
+    # (d) vision RoPE head_dim 80 on [16384, 16, 80] q / k views of a packed qkv
+    qkv = rn(g, 16384, 3, 16, 80)
+    qd, kd, _ = qkv.unbind(1)
+    f = torch.randn(16384, 40, generator=g).to(dev)
+    emb = torch.cat((f, f), -1)
+    vc, vs = emb.cos(), emb.sin()
+    orig_vis = getattr(hf.apply_rotary_pos_emb_vision, "_umic_original",
+                       hf.apply_rotary_pos_emb_vision)
+    hbm_entry("cfg2d_vision_rope", lambda: apply_rotary_vision(qd, kd, vc, vs),
+              lambda: orig_vis(qd, kd, vc, vs),
+              2 * 2 * 16384 * 16 * 80 * 2 + 2 * 16384 * 80 * 4)
+    out["note"] = ("median of CUDA-event times, each call after a 256 MB L2-flushing write; "
+                   "eager = unfused torch / HF functions on the same GPU")
+    return out
+
+
+def _fp32_vision(vis, pix, grid) -> torch.Tensor:
+    import copy
+
+    prev = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = torch.backends.cudnn.allow_tf32 = False
+    try:
+        vis32 = copy.deepcopy(vis).float()
+        with torch.no_grad():
+            out = vis32(pix.float(), grid_thw=grid).last_hidden_state
+        del vis32
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = prev
 
 
 def _prefix_cache(layers: int, episodes: int, heads: int, tokens: int, dim: int, dev,
@@ -99,6 +238,7 @@ def measure_flow(dev: torch.device, episodes: int = 32, tokens: int = 64,
     cache = _prefix_cache(cfg["num_hidden_layers"], episodes, heads_kv, prefix, head_dim, dev)
     eager_ms = _timed(lambda: flow_sample(expert, cache, prefix, x0), warmup=1)
     ref = flow_sample(expert, cache, prefix, x0)
+    ref32 = _fp32_flow(expert, cfg, episodes, prefix, x0, dev)
     holder = AlpamayoStandIn(torch.nn.Module(), expert=expert)
     apply(holder, UmicConfig(decode_graph=False, decode_cache=False))
     try:
@@ -111,12 +251,43 @@ def measure_flow(dev: torch.device, episodes: int = 32, tokens: int = 64,
     return {"episodes": episodes, "action_tokens": tokens, "prefix_tokens": prefix,
             "euler_steps": FLOW_STEPS, "eager_ms": eager_ms, "ms": ours_ms,
             "graph_ms": graph_ms, "speedup": eager_ms / min(ours_ms, graph_ms),
-            "rel_err_vs_eager": _rel(got, ref)}
+            "rel_err_vs_eager": _rel(got, ref),
+            "rel_err_vs_fp32": {"ours": _rel(got, ref32), "eager": _rel(ref, ref32)}}
+
+
+def _fp32_flow(expert, cfg, episodes, prefix, x0, dev) -> torch.Tensor:
+    """The same flow run on an fp32 copy of the expert and of the prefix cache (TF32 off)."""
+    import copy
+
+    prev = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = torch.backends.cudnn.allow_tf32 = False
+    try:
+        ex32 = copy.deepcopy(expert).float()
+        cache = _prefix_cache(cfg["num_hidden_layers"], episodes, cfg["num_key_value_heads"],
+                              prefix, cfg["head_dim"], dev)
+        for lyr in cache.layers:
+            lyr.keys, lyr.values = lyr.keys.float(), lyr.values.float()
+        out = flow_sample(ex32, cache, prefix, x0.float())
+        del ex32, cache
+        torch.cuda.empty_cache()
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = prev
+
+
+def _peaks() -> dict:
+    from pathlib import Path
+
+    p = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    return json.loads(p.read_text()) if p.exists() else {"hbm_gbs": 6650.0,
+                                                         "bf16_tflops": 1590.0}
 
 
 def main() -> None:
     dev = torch.device("cuda", torch.cuda.current_device())
-    out = {"vision": measure_vision(dev)}
+    out = {"kernels": measure_kernels(dev, _peaks())}
+    torch.cuda.empty_cache()
+    out["vision"] = measure_vision(dev)
     torch.cuda.empty_cache()
     out["flow"] = measure_flow(dev)
     print(json.dumps(out), flush=True)

@@ -61,6 +61,38 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
     return normed.reshape(shape), summed.reshape(shape)
 
 
+def rmsnorm_axpy(x: torch.Tensor, weight: torch.Tensor, eps: float, base: torch.Tensor,
+                 alpha: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """base + alpha * rmsnorm(x) * weight in one pass (fp32 inside, one bf16 rounding).
+
+    The Euler update x + dt * v of the flow sampler when the velocity v is an RMSNorm
+    output. `out` may be `base` itself for an in-place update; by default a new tensor
+    of base's shape is returned."""
+    dev = require_cuda("rmsnorm_axpy", x, weight, base, out)
+    require_bf16("rmsnorm_axpy", x, base, out)
+    if base.shape != x.shape:
+        raise ValueError(f"rmsnorm_axpy: shapes differ {tuple(x.shape)} vs {tuple(base.shape)}")
+    x2d, n = rows_view(x)
+    b2d, _ = rows_view(base)
+    w = weight.contiguous()
+    if w.numel() != n:
+        raise ValueError(f"rmsnorm_axpy: weight has {w.numel()} elements, rows have {n}")
+    rows = x2d.shape[0]
+    if out is None:
+        y = torch.empty((rows, n), device=x.device, dtype=x.dtype)
+    else:
+        if out.shape != x.shape:
+            raise ValueError("rmsnorm_axpy: out must have x's shape")
+        y, _ = rows_view(out)
+        if out.numel() and y.data_ptr() != out.data_ptr():
+            raise ValueError("rmsnorm_axpy: out must be row-addressable in place")
+    _lib.call("umic_rmsnorm_axpy", dev, x2d.data_ptr(), row_stride(x2d), w.data_ptr(),
+              _w_dtype(w), b2d.data_ptr(), row_stride(b2d), float(alpha), y.data_ptr(),
+              row_stride(y), rows, n, float(eps))
+    stats["umic_rmsnorm_axpy"] += 1
+    return out if out is not None else y.reshape(x.shape)
+
+
 # Names of the reference interface (src/umic/kernels/rmsnorm.py:53,103).
 rmsnorm_triton = rmsnorm
 add_rmsnorm_triton = add_rmsnorm

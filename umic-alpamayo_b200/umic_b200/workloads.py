@@ -224,17 +224,28 @@ def flow_sample(expert: nn.Module, cache, base_len: int, x0: torch.Tensor,
                 steps: int = FLOW_STEPS, graph: bool = False) -> torch.Tensor:
     """Euler integration x <- x + dt * v(x) over `steps` steps.
 
+    When apply() has rebound the expert's final RMSNorm, the update runs inside that
+    norm's kernel (integrate.axpy_epilogue): a step is the expert pass and nothing else.
+
     graph=True runs the steps through FlowStepGraph (the reference's unwired
     graph.py:179-253): after two eager warm-up steps one whole Euler step -- the
     expert pass with its prefix-KV append and crop, and the update x + dt * v --
     is captured once as a CUDA graph and replayed (same shapes and buffer
     addresses every step; only x changes). The runner is kept on the expert per
     (shape, dtype, cache, prefix length, steps), so later calls replay every step."""
+    from . import integrate
     from .graph import FlowStepGraph
 
     dt = 1.0 / steps
+    final_norm = getattr(expert, "norm", None)
+    fused_update = integrate.has_axpy_epilogue(final_norm)
 
     def euler(x: torch.Tensor, t: torch.Tensor | None) -> torch.Tensor:
+        if fused_update:
+            # the velocity is the expert's final RMSNorm output: that kernel writes
+            # x + dt * v directly (umic_rmsnorm_axpy), v is never stored
+            with integrate.axpy_epilogue(final_norm, x, dt):
+                return flow_step(expert, cache, base_len, x)
         return x + dt * flow_step(expert, cache, base_len, x)
 
     x = x0
