@@ -1,6 +1,6 @@
 """Single-kernel micro-benchmark of the library against cuBLAS / eager torch.
 
-    python -m umic_b200.kernel_bench [--out results.json]
+    python kernel_bench.py [--out results.json]
 
 Each case is timed with CUDA events around one launch after 3 warm-up launches,
 with a 256 MB buffer read between launches to flush L2 (a read leaves no dirty
@@ -10,8 +10,15 @@ against cuBLAS on the same inputs. The decode GEMV shapes are also timed back to
 back over enough weight copies to exceed L2 (the regime of a decode step), for
 the streaming engine (with a workspace) and the cluster engine (without).
 """
+
 import json
 import sys
+from pathlib import Path
+
+_ROOT = Path(__file__).resolve().parent
+for _p in (_ROOT, _ROOT / "umic-alpamayo_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
 
 import torch
 

@@ -1,6 +1,6 @@
 """Runs one kernel of the library a few times on a BASELINE shape (profiling driver).
 
-    python -m umic_b200.kernel_driver <mode> [rows] [--iters N] [--time]
+    python kernel_driver.py <mode> [rows] [--iters N] [--time]
 
 Used to capture a single kernel under ncu. Modes and shapes:
   dual           gate/up dual-accumulator GEMM, x [rows=24800, 4096], W [12288, 4096] x 2
@@ -23,9 +23,17 @@ Inputs are seeded random tensors created on cuda:0 before the launches. --time r
 (the inputs of the attention modes exceed L2), printing microseconds per launch.
 """
 
+
 from __future__ import annotations
 
 import argparse
+import sys
+from pathlib import Path
+
+_ROOT = Path(__file__).resolve().parent
+for _p in (_ROOT, _ROOT / "umic-alpamayo_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
 
 import torch
 

@@ -1,10 +1,10 @@
 """Generates the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a container where the reference project is importable (its source tree
-at REF_SRC, default /root/reference/src); the fixtures are committed, so the
-tests never need the reference at run time:
+Run where the reference project's source tree is available, naming its `src`
+directory with --ref-src or the UMIC_REF_SRC environment variable; the fixtures
+are committed, so the tests never need the reference at run time:
 
-    python tests/golden/make_golden.py [--ref-src PATH]
+    python tests/golden/make_golden.py --ref-src <reference>/src
 
 What is recorded (small seeded cases, CPU):
   * outputs of the reference's own Triton kernels run by Triton's CPU
@@ -202,8 +202,11 @@ def matcher_counts() -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-src", default="/root/reference/src")
+    ap.add_argument("--ref-src", default=os.environ.get("UMIC_REF_SRC"),
+                    help="the reference project's src directory (or set UMIC_REF_SRC)")
     args = ap.parse_args()
+    if not args.ref_src:
+        ap.error("name the reference's src directory with --ref-src or UMIC_REF_SRC")
     sys.path.insert(0, args.ref_src)
     import torch
 

@@ -108,3 +108,18 @@ def test_binding_arity_matches_header():
         assert m, name
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), f"{name}: header {len(params)} vs binding {len(args)}"
+
+
+@pytest.mark.parametrize("o_st", [0, -2048, 12])
+def test_attention_rows_rejects_bad_output_strides_on_host(o_st):
+    """Output strides must be positive multiples of 8 like the input strides: a zero or
+    negative stride would make rows overwrite one another or write before the buffer."""
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)  # never dereferenced: the stride check fails first
+    rc = L.umic_attention_rows(fake, 8 * 16 * 64 * 128, 64 * 128, 128,
+                               fake, 8 * 64 * 128, 64 * 128, 128,
+                               fake, 8 * 64 * 128, 64 * 128, 128, None, 0, 0, 0,
+                               fake, 64 * 16 * 128, 128, o_st, 1, 16, 8, 64, 64, 128,
+                               ctypes.c_float(0.1), None)
+    assert rc == 3
+    assert "strides" in _lib.last_message()

@@ -672,7 +672,7 @@ extern "C" int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, in
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !stride_ok(q_sh) ||
       !stride_ok(q_st) || !stride_ok(q_sb) || !stride_ok(k_sl) || !stride_ok(k_sh) ||
       !stride_ok(k_sb) || !stride_ok(v_sl) || !stride_ok(v_sh) || !stride_ok(v_sb) ||
-      o_sb % 8 || o_sh % 8 || o_st % 8)
+      !stride_ok(o_sb) || !stride_ok(o_sh) || !stride_ok(o_st))
     return fail(UMIC_ERR_ALIGNMENT, "%s: 16-byte aligned bases and strides required", kName);
   if (mask_bits && (m_sb < 0 || m_sh < 0 || m_st < 0))
     return fail(UMIC_ERR_INVALID_ARG, "%s: negative mask stride", kName);
