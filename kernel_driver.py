@@ -12,6 +12,8 @@ Used to capture a single kernel under ncu. Modes and shapes:
   rope_text      q [3100, 32, 128], k [3100, 8, 128], bf16 tables   (cfg2c)
   rope_vision    q, k [16384, 16, 80] views of qkv, fp32 tables     (cfg2d)
   gemv           x [rows=8, 4096], W [12288, 4096]
+  vit            the cfg3 encoder after apply(), rows = images (16)
+  decode         one graph-replayed cfg4 decode step of rows = 8 episodes
   kv             K/V [8, 8, 3100, 128] appended into [8, 8, 3172, 128]
   attn           flow-step attention: q [rows=32 episodes, 16, 64, 128] over the
                  3164-key prefix of a [32, 8, 3172, 128] cache, lower-right causal mask
@@ -39,9 +41,10 @@ import torch
 
 
 def make(mode: str, rows: int | None):
-    from .kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inplace,
-                          apply_rotary_vision, gate_silu_mul_nk, kv_append, linear, linear_gemv)
-    from .kernels.attention import qk_norm_rope_kv
+    from umic_b200.kernels import (add_layernorm, add_rmsnorm, apply_rotary_text_inplace,
+                                   apply_rotary_vision, gate_silu_mul_nk, kv_append, linear,
+                                   linear_gemv)
+    from umic_b200.kernels.attention import qk_norm_rope_kv
 
     dev = torch.device("cuda", 0)
     bf = torch.bfloat16
@@ -98,7 +101,7 @@ def make(mode: str, rows: int | None):
         w = torch.randn(12288, 4096, device=dev, dtype=bf)
         return lambda: linear_gemv(x, w)
     if mode in ("attn", "attn_nomask", "attn_sdpa"):
-        from .kernels.attention import attention_rows
+        from umic_b200.kernels.attention import attention_rows
 
         b, hq, hk, t, lk, cap, d = (rows or 32), 16, 8, 64, 3164, 3172, 128
         q = torch.randn(b, t, hq, d, device=dev, dtype=bf).transpose(1, 2)
@@ -119,6 +122,45 @@ def make(mode: str, rows: int | None):
         kn = torch.randn(8, 3100, 8, 128, device=dev, dtype=bf).transpose(1, 2)
         vn = torch.randn_like(kn)
         return lambda: kv_append(kb, vb, kn, vn, 0)
+    if mode == "vit":  # the whole cfg3 encoder (16 images) after apply(): one forward a call
+        from umic_b200 import UmicConfig, apply
+        from umic_b200.workloads import build_vision_model, vit_inputs
+
+        vis = build_vision_model(device=dev)
+        pix, grid = vit_inputs(images=rows or 16, device=dev)
+        holder = torch.nn.Module()
+        holder.vlm = torch.nn.Module()
+        holder.vlm.visual = vis
+        apply(holder, UmicConfig(decode_graph=False, decode_cache=False, decode_gemv=False))
+
+        def vit():
+            with torch.no_grad():
+                vis(pix, grid_thw=grid)
+        return vit
+    if mode == "decode":  # one cfg4 decode step of `rows` episodes (graph replay) per call
+        from umic_b200 import UmicConfig, apply
+        from umic_b200.workloads import AlpamayoStandIn, build_vlm, kv_cache_for, prefill_ids
+
+        b = rows or 8
+        vlm = build_vlm(device=dev, seed=4)
+        ids = prefill_ids(b, 3100, seed=4, device=dev)
+        model = AlpamayoStandIn(vlm)
+        apply(model, UmicConfig(max_new_tokens=80))
+        cache = kv_cache_for(vlm, b, 3100 + 80, dev)
+        runner = model._umic_decode_runner
+        with torch.no_grad():
+            out = vlm(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        tok = out.logits[:, -1].argmax(-1)[:, None]
+        base = cache.get_seq_length()
+
+        def step():
+            # the same KV length each call: after the runner's two warm-up steps every call
+            # replays one captured graph
+            if runner.in_decode:
+                cache.set_pos(base)
+            with torch.no_grad():
+                vlm(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        return step
     raise SystemExit(f"unknown mode {mode}")
 
 
