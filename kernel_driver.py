@@ -20,7 +20,9 @@ Used to capture a single kernel under ncu. Modes and shapes:
                  (mask packing + umic_attention_rows)
   attn_nomask    the same without a mask
   attn_sdpa      the same shape and mask through torch SDPA (what transformers runs)
-Inputs are seeded random tensors created on cuda:0 before the launches. --time runs
+Inputs are seeded random tensors created on cuda:0 before the launches. Without --time
+the first call runs alone and the next --iters calls run inside the NVTX range "drv"
+(`ncu --nvtx --nvtx-include "drv/"` captures just those). --time runs
 3 warm-up launches and then times --iters launches back to back with CUDA events
 (the inputs of the attention modes exceed L2), printing microseconds per launch.
 """
@@ -185,9 +187,13 @@ def main() -> None:
         print(f"{a.mode}: {s.elapsed_time(e) * 1e3 / a.iters:.1f} us per launch "
               f"({a.iters} back to back)")
         return
+    fn()  # first call outside the range: lazy initialisation, graph capture
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("drv")  # ncu --nvtx --nvtx-include "drv/" selects these calls
     for _ in range(a.iters):
         fn()
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     print("ok", a.mode)
 
 

@@ -6,12 +6,16 @@
 // Both operands are K-major (activations [m, k] row-major, nn.Linear weights
 // [n, k] row-major), so no transpose or copy of the weights is ever made.
 //
-// Persistent kernel, one CTA per SM, 6 warps with fixed roles:
-//   warp 0     TMA producer: fills a 4-stage shared-memory ring of
-//              (A 128x64, B 256x64) bf16 tiles, 128-byte swizzled;
-//   warp 1     allocates 512 TMEM columns; one lane issues tcgen05.mma
-//              (M=128, N=256, K=16; 4 per 64-wide k-block) and commits each
-//              stage back to the producer through an mbarrier;
+// Persistent kernel, one CTA per SM, 6 warps with fixed roles. For m > 128 the CTAs
+// run as pairs (cta_group::2): a pair computes a 256 x 256 tile with one M = 256,
+// N = 256, K = 16 MMA per 16-wide k-step, each CTA staging its 128 rows of A and half
+// of B; one-block shapes (m <= 128) use single CTAs with M = 128 tiles.
+//   warp 0     TMA producer: fills the shared-memory ring (6 stages of 32 KB per
+//              CTA for pairs: A 128x64 + B 128x64; 4 stages of 48 KB for single
+//              CTAs: A 128x64 + B 256x64), bf16, 128-byte swizzled;
+//   warp 1     allocates 512 TMEM columns; in the pair's leader CTA one lane issues
+//              tcgen05.mma (4 per 64-wide k-block) and commits each stage back to
+//              both CTAs' producers through their mbarriers;
 //   warps 2-5  epilogue: tcgen05.ld of the fp32 accumulator (each warp reads
 //              its 32-lane TMEM quarter), bias / activation / residual in
 //              registers, then the bf16 32 x 32 chunk is staged in shared
@@ -206,9 +210,17 @@ __device__ __forceinline__ void tile_coords(int t, const TcParams& p, int& mb, i
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
 }
+// tanh on the SFU (PTX tanh.approx.f32, relative error about 2^-11, far below the bf16
+// rounding of the output): the ViT fc1 epilogue evaluates one per element, and the
+// multi-instruction library tanhf left that epilogue longer than the tile's MMAs at K = 1280.
+__device__ __forceinline__ float tanh_sfu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.f + tanhf(u));
+  return 0.5f * x * (1.f + tanh_sfu(u));
 }
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 

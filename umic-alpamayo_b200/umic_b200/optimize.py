@@ -116,8 +116,14 @@ def _vision_phase(visual: nn.Module, cfg: UmicConfig, report: dict) -> None:
     report["ve_pipeline_fused"] = integrate.fuse_vision_encoder_pipeline(visual)
     if cfg.vision_gemm_fusion:
         # fc1 with the tanh-GELU in the GEMM epilogue (the reference's epilogue was erf
-        # only, so it left the ViT MLPs on cuBLAS, src/umic/integrate.py:93-95)
+        # only, so it left the ViT MLPs on cuBLAS, src/umic/integrate.py:93-95), and the
+        # attention's qkv projection with its bias in the epilogue (the site the reference
+        # measured its own kernel winning, 1.23 vs 2.22 ms, but left off by default).
+        # fc2 and proj (N = 1280: five column tiles for 74 CTA pairs) stay on cuBLAS,
+        # which is faster at that width.
         report["ve_gelu_mlp_fused"] = integrate.fuse_gelu_mlps(visual)
+        report["ve_linear_fused"] = integrate.fuse_linears(visual,
+                                                           names=integrate.VIT_LINEAR_NAMES)
 
 
 def _expert_phase(expert: nn.Module, cfg: UmicConfig, report: dict) -> None:
