@@ -123,3 +123,10 @@ def test_attention_rows_rejects_bad_output_strides_on_host(o_st):
                                ctypes.c_float(0.1), None)
     assert rc == 3
     assert "strides" in _lib.last_message()
+
+
+def test_debug_stall_rejects_bad_arguments():
+    L = _lib.lib()
+    assert L.umic_debug_stall(0, 1000) == 1
+    assert L.umic_debug_stall(1, 0) == 1
+    assert "umic_debug_stall" in _lib.last_message()

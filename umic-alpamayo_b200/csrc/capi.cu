@@ -1,5 +1,6 @@
 // Library-wide state of the C ABI: error messages, the device error word and
 // per-device attribute caches.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -17,6 +18,9 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 uint32_t* g_err_ptr[kMaxDevices] = {nullptr};
 int g_sms[kMaxDevices] = {0};
+
+std::atomic<int> g_stall_kernel{0};
+std::atomic<long long> g_stall_limit{0};
 
 int current_device() {
   int d = 0;
@@ -65,9 +69,25 @@ int sm_count() {
   return g_sms[d];
 }
 
+bool take_stall(int kernel, long long* limit) {
+  int expected = kernel;
+  if (!g_stall_kernel.compare_exchange_strong(expected, 0)) return false;
+  *limit = g_stall_limit.load();
+  return true;
+}
+
 }  // namespace umic
 
 extern "C" {
+
+int umic_debug_stall(int kernel, int64_t wait_limit_cycles) {
+  if (kernel < umic::kStallGemm || kernel > umic::kGemvGeneralMerge || wait_limit_cycles <= 0)
+    return umic::fail(UMIC_ERR_INVALID_ARG, "umic_debug_stall: kernel %d, limit %lld", kernel,
+                      (long long)wait_limit_cycles);
+  umic::g_stall_limit.store(wait_limit_cycles);
+  umic::g_stall_kernel.store(kernel);
+  return UMIC_OK;
+}
 
 int umic_abi_version(void) { return 2; }
 

@@ -27,6 +27,13 @@ uint32_t* device_error_word();
 // Streaming multiprocessor count of the current device (cached per device).
 int sm_count();
 
+// Test hook of the bounded-wait abort path (umic_debug_stall): true, with the armed wait
+// limit in *limit, exactly once after `kernel` was armed; false otherwise.
+constexpr int kStallGemm = 1;
+constexpr int kStallGemv = 2;
+constexpr int kGemvGeneralMerge = 3;  // not a stall: the next GEMV skips its fast merge
+bool take_stall(int kernel, long long* limit);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }

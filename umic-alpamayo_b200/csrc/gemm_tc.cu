@@ -84,6 +84,8 @@ struct TcParams {
   int tiles_m, tiles_n;  // output tiles
   int kblocks;
   int epilogue;
+  long long wait_limit;  // SM cycles a bounded wait may take before the CTA unwinds
+  int stall;             // test hook: CTA 0 skips the loads of its first stage
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -310,17 +312,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           row_b = nb * kBN + static_cast<int>(rank) * (kBN / kPair);
         }
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag)) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag, p.wait_limit)) {
             ok = false;
             break;
           }
           const uint32_t sa = sbase + stage * G::kStageBytes;
           const uint32_t sb = sa + kABytes;
+          // Test hook (umic_debug_stall): the stage's bytes are announced but CTA 0 never
+          // loads them, so the MMA's wait on it runs out and the abort path unwinds.
+          const bool skip = p.stall && blockIdx.x == 0 && !issued;
           if constexpr (kPair == 2) {
             const uint32_t fb = lead_full0 + 8 * stage;
             if (leader) mbar_expect_tx(full0 + 8 * stage, 2 * G::kStageBytes);
-            tma_load_2d_pair(sa, &map_a, fb, kb * kBK, row_a);
-            tma_load_2d_pair(sb, bmap, fb, kb * kBK, row_b);
+            if (!skip) {
+              tma_load_2d_pair(sa, &map_a, fb, kb * kBK, row_a);
+              tma_load_2d_pair(sb, bmap, fb, kb * kBK, row_b);
+            }
+          } else if (skip) {
+            mbar_expect_tx(full0 + 8 * stage, G::kStageBytes);
           } else {
             const uint32_t fb = full0 + 8 * stage;
             mbar_expect_tx(fb, G::kStageBytes);
@@ -343,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Tail: wait until the MMA has released every stage this CTA filled, so no
         // commit from the (possibly peer) MMA thread is still in flight at exit.
         for (int s = 0; s < G::kStages; ++s) {
-          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag)) break;
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag, p.wait_limit)) break;
           if (++stage == G::kStages) {
             stage = 0;
             phase ^= 1;
@@ -369,14 +378,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = unit; t < tiles && ok; t += units, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, p.err, abort_flag)) {
+        if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, p.err, abort_flag, p.wait_limit)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * kBN;
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(full0 + 8 * stage, phase, p.err, abort_flag)) {
+          if (!mbar_wait(full0 + 8 * stage, phase, p.err, abort_flag, p.wait_limit)) {
             ok = false;
             break;
           }
@@ -402,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Wait for every MMA issued by this thread before TMEM is released.
       mma_commit<kPair>(drain);
-      mbar_wait(drain, 0, p.err, abort_flag);
+      mbar_wait(drain, 0, p.err, abort_flag, p.wait_limit);
     }
     __syncwarp();
   } else {
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(t, p, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(accf0 + 8 * acc, acc_phase, p.err, abort_flag)) break;
+      if (!mbar_wait(accf0 + 8 * acc, acc_phase, p.err, abort_flag, p.wait_limit)) break;
       tc_fence_after();
       const int row = mb * G::kTileM + static_cast<int>(rank) * kBM + quarter * 32 + lane;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
@@ -594,6 +603,15 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   p.tiles_n = static_cast<int>((n + out_cols - 1) / out_cols);
   p.kblocks = static_cast<int>((k + kBK - 1) / kBK);
   p.epilogue = epilogue;
+  p.wait_limit = kWaitLimitCycles;
+  p.stall = 0;
+  {
+    long long limit = 0;
+    if (take_stall(kStallGemm, &limit)) {
+      p.stall = 1;
+      p.wait_limit = limit;
+    }
+  }
   const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x7fffffffLL) return fail(UMIC_ERR_UNSUPPORTED, "%s: too many tiles", name);
   const int sms = sm_count();

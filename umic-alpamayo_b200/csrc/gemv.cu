@@ -314,6 +314,9 @@ struct StreamArgs {
   // Optional residual added in the epilogue of a single plain GEMV: y = W x + res.
   const __nv_bfloat16* res;
   int64_t ldres;
+  long long wait_limit;  // SM cycles a bounded wait may take before the CTA unwinds
+  int stall;             // test hook: CTA 0 skips the loads of its first unit
+  int no_fast;           // test hook: every split row block takes the general merge
 };
 
 __device__ __forceinline__ int st_unit_begin(int c, const StreamArgs& a) {
@@ -389,14 +392,17 @@ __global__ void __launch_bounds__(kStThreads, 1)
         const int si = st_segment(rb * kStRows, a);
         const CUtensorMap* map = si == 0 ? &m0 : (si == 1 ? &m1 : &m2);
         const int rin = rb * kStRows - a.row0[si];
-        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, a.err, flags)) {
+        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, a.err, flags, a.wait_limit)) {
           ok = false;
           break;
         }
         const uint32_t fb = full0 + 8 * stage;
         const uint32_t dst = sbase + stage * kStStageBytes;
         mbar_expect_tx(fb, kStStageBytes);  // out-of-range rows / columns arrive as zeros
-        if constexpr (kGated) {
+        if (a.stall && c == 0 && u == u0) {
+          // Test hook (umic_debug_stall): the bytes are announced but never loaded, so the
+          // consumers' wait on this stage runs out and the CTA unwinds.
+        } else if constexpr (kGated) {
           tma_load_2d(dst, &m0, fb, kc * kKC, rin);
           tma_load_2d(dst + 8192, &m0, fb, kc * kKC + 64, rin);
           tma_load_2d(dst + 16384, &m1, fb, kc * kKC, rin);
@@ -414,7 +420,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
       if (ok) {
         // Every stage released by the consumers before the CTA may exit.
         for (int s = 0; s < kStStages; ++s) {
-          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, a.err, flags)) break;
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, a.err, flags, a.wait_limit)) break;
           if (++stage == kStStages) {
             stage = 0;
             phase ^= 1;
@@ -605,7 +611,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
         zero_acc();
       }
       cur = rb;
-      if (rb == rb_last) try_fast(rb);
+      if (rb == rb_last && !a.no_fast) try_fast(rb);
     }
     // this chunk's activations, requested before the weights land
     uint4 xv[kSlabs][MC];
@@ -621,7 +627,7 @@ __global__ void __launch_bounds__(kStThreads, 1)
     }
     // Every consumer warp passes or fails the same waits, so none is left alone at a
     // named barrier when another gives up.
-    if (!mbar_wait(full0 + 8 * stage, phase, a.err, flags)) return;
+    if (!mbar_wait(full0 + 8 * stage, phase, a.err, flags, a.wait_limit)) return;
     const uint32_t st = sbase + stage * kStStageBytes;
 #pragma unroll
     for (int s = 0; s < kSlabs; ++s) {
@@ -726,6 +732,16 @@ int stream_launch(const char* name, const GemvArgs& a, void* ws, size_t ws_bytes
   s.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + stream_counter_offset());
   s.err = device_error_word();
   s.weights_ready = (flags & UMIC_GEMV_WEIGHTS_READY) ? 1 : 0;
+  s.wait_limit = kWaitLimitCycles;
+  s.stall = 0;
+  {
+    long long limit = 0;
+    if (take_stall(kStallGemv, &limit)) {
+      s.stall = 1;
+      s.wait_limit = limit;
+    }
+    s.no_fast = take_stall(kGemvGeneralMerge, &limit) ? 1 : 0;
+  }
   if (extra) {  // residual epilogue
     s.res = extra->res;
     s.ldres = extra->ldres;

@@ -50,14 +50,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (after flagging the error word and the CTA abort flag) if it never does.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t* err,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try(bar, parity)) return true;
   const long long start = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort_flag) return false;
-      if (clock64() - start > kWaitLimitCycles) {
+      if (clock64() - start > limit) {
         *abort_flag = 1;
         if (err) atomicOr(err, UMIC_DEVERR_WAIT_TIMEOUT);
         return false;

@@ -31,6 +31,7 @@ _SIGNATURES: dict[str, list] = {
     "umic_last_error_message": [],
     "umic_set_device": [_c_int],
     "umic_device_errors": [ctypes.POINTER(ctypes.c_uint32), _c_int],
+    "umic_debug_stall": [_c_int, _c_i64],
     "umic_rmsnorm": [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_i64, _c_i64, _c_f32, _c_p],
     "umic_rmsnorm_axpy": [_c_p, _c_i64, _c_p, _c_int, _c_p, _c_i64, _c_f32, _c_p, _c_i64,
                           _c_i64, _c_i64, _c_f32, _c_p],
@@ -168,6 +169,24 @@ def device_errors(device: torch.device | None = None, clear: bool = True) -> int
     if rc:
         raise UmicError("umic_device_errors", rc, last_message())
     return int(v.value)
+
+
+def arm_stall(kernel: int, wait_limit_cycles: int) -> None:
+    """Test hook: the next launch of `kernel` (1 = GEMM, 2 = streaming GEMV) stalls one CTA
+    and unwinds after `wait_limit_cycles`; 3 makes the next streaming GEMV merge split row
+    blocks only through its general path (see umic_debug_stall in the header)."""
+    rc = lib().umic_debug_stall(kernel, wait_limit_cycles)
+    if rc:
+        raise UmicError("umic_debug_stall", rc, last_message())
+
+
+def zero_gemv_workspaces() -> None:
+    """Zeroes every streaming-GEMV workspace of this process (needed after a launch that
+    unwound on a wait timeout: its row-block counters may be left non-zero)."""
+    for buf in _workspaces.values():
+        buf.zero_()
+    for dev_idx in _workspaces:
+        torch.cuda.synchronize(dev_idx)
 
 
 def ptr(t: torch.Tensor | None) -> int | None:
