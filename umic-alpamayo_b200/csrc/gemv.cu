@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "mma_frag.cuh"
 #include "tma.cuh"
 
 namespace umic {
@@ -51,23 +52,6 @@ struct GemvArgs {
   int m, n, k;  // n = total rows over the segments
   int slabs;    // ceil(k / 32)
 };
-
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Two k16 steps from one 32-wide slab: rows g / g+8 of w (wlo / whi) and
-// row g of x, each 8 consecutive k values held as a uint4.
-__device__ __forceinline__ void slab_mma(float (&c)[4], const uint4& wlo, const uint4& whi,
-                                         const uint4& xv) {
-  mma16816(c, wlo.x, whi.x, wlo.y, whi.y, xv.x, xv.y);
-  mma16816(c, wlo.z, whi.z, wlo.w, whi.w, xv.z, xv.w);
-}
 
 namespace cg = cooperative_groups;
 
@@ -325,17 +309,6 @@ __device__ __forceinline__ int st_unit_begin(int c, const StreamArgs& a) {
 // CTA whose range holds unit u.
 __device__ __forceinline__ int st_cta_of(int u, const StreamArgs& a) {
   return static_cast<int>(((static_cast<long long>(u) + 1) * a.ctas + a.units - 1) / a.units) - 1;
-}
-// Byte address of 16-byte chunk `chunk` of row r in a 128-byte-swizzled [64 x 64] box.
-__device__ __forceinline__ uint32_t st_swz(uint32_t box, int r, int chunk) {
-  return box + r * 128 + ((chunk ^ (r & 7)) << 4);
-}
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
-  return v;
 }
 __device__ __forceinline__ int st_segment(int row, const StreamArgs& a) {
   int si = 0;
