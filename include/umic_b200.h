@@ -318,42 +318,6 @@ UMIC_API int umic_gemv_gate_silu_mul(const void* x, int64_t ldx, const void* wg,
                                      int64_t k, void* workspace, size_t workspace_bytes,
                                      uint32_t flags, void* stream);
 
-/* The decode step's MLP half of one decoder layer as ONE persistent kernel, for m <= 16
- * rows (one token per episode):
- *   o      = attn . w_o^T                                   (o_proj, no bias)
- *   summed = o + residual;  normed = RMSNorm(summed) * post_w   (post_attention_layernorm)
- *   h      = silu(normed . w_gate^T) * (normed . w_up^T)
- *   out    = h . w_down^T + summed                          (down_proj + the MLP residual)
- * The three weight streams are phases of one cooperative launch (one CTA per SM): the TMA
- * ring of each CTA keeps streaming the next phase's weights while the grid waits at the
- * phase boundary (a bounded grid barrier; the add+RMSNorm runs on the CTA that arrives
- * last). Same result as umic_gemv (o_proj) -> umic_add_rmsnorm -> umic_gemv_gate_silu_mul ->
- * umic_gemv_residual with a workspace, bit for bit.
- * attn [m, k_attn] (ld_attn), residual and out [m, hidden] (ld_res must equal hidden),
- * w_o [hidden, k_attn], w_gate / w_up [inter, hidden] (one ld_wgu), w_down [hidden, inter];
- * hidden and inter multiples of 64. scratch: at least 3 * align256(m * hidden * 2) +
- * align256(m * inter * 2) bytes, 16-byte aligned (the o, normed, summed and h rows).
- * workspace: umic_decode_chain_workspace_bytes() bytes, 256-byte aligned, zero-filled
- * before its first use; each call leaves it zeroed (after a call that set
- * UMIC_DEVERR_WAIT_TIMEOUT, zero it again). Calls sharing a workspace must be ordered on
- * one stream. Shapes it does not cover return UMIC_ERR_UNSUPPORTED.
- * Replaces, for decode rows, o_proj (_patched_linear_forward, integrate.py:98-107), the
- * attention-residual add + post_attention_layernorm (integrate.py:180-209 with
- * add_rmsnorm_triton, rmsnorm.py:103-134) and the MLP with its residual
- * (_fused_mlp_forward, integrate.py:44-55, whose rows < FUSE_MIN_ROWS branch ran eager). */
-UMIC_API int umic_decode_mlp_chain(const void* attn, int64_t ld_attn, const void* w_o,
-                                   int64_t ld_wo, const void* residual, int64_t ld_res,
-                                   const void* post_w, int post_w_dtype, float post_eps,
-                                   const void* w_gate, const void* w_up, int64_t ld_wgu,
-                                   const void* w_down, int64_t ld_wd, void* out, int64_t ld_out,
-                                   void* scratch, size_t scratch_bytes, int64_t m,
-                                   int64_t hidden, int64_t k_attn, int64_t inter,
-                                   void* workspace, size_t workspace_bytes, void* stream);
-
-/* Bytes of workspace umic_decode_mlp_chain needs (fixed: per-CTA partial slots for up to
- * 256 SMs, row-block counters for 262144 rows per phase, the phase barrier counters). */
-UMIC_API size_t umic_decode_chain_workspace_bytes(void);
-
 /* Tensor-core (tcgen05 + TMEM, TMA-fed) GEMM: y = epi(x . w^T + bias) + residual.
  * x [m, k], w [n, k] (both K-major), y [m, n]. bias / residual may be NULL.
  * epilogue: UMIC_EPI_*. Requires k % 8 == 0, n % 8 == 0, leading dimensions that

@@ -112,7 +112,6 @@ def test_cfg4_greedy_token_stream(cuda):
         stats.clear()
         tok_o, l_o = _stream(vlm, ids, steps, cache)
         assert stats["umic_gemm_gate_silu_mul"] >= 36 and stats["umic_qk_norm_rope_kv"] >= 36
-        assert stats["umic_decode_mlp_chain"] >= 36  # decode steps: one launch per layer tail
         cache.crop(0)
         tok_o2, l_o2 = _stream(vlm, ids, steps, cache)  # every step a graph replay
         cache.crop(0)

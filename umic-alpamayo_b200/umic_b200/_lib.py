@@ -69,17 +69,12 @@ _SIGNATURES: dict[str, list] = {
                             _c_f32, _c_p],
     "umic_mask_pack_bits": [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
                             _c_i64, _c_i64, _c_i64, _c_p],
-    "umic_decode_mlp_chain": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_int, _c_f32,
-                              _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_size,
-                              _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_size, _c_p],
-    "umic_decode_chain_workspace_bytes": [],
     "umic_gemm": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64,
                   _c_i64, _c_int, _c_p],
     "umic_gemm_gate_silu_mul": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64,
                                 _c_i64, _c_i64, _c_p],
 }
-_RESTYPES = {"umic_last_error_message": ctypes.c_char_p, "umic_gemv_workspace_bytes": _c_size,
-             "umic_decode_chain_workspace_bytes": _c_size}
+_RESTYPES = {"umic_last_error_message": ctypes.c_char_p, "umic_gemv_workspace_bytes": _c_size}
 
 ERR_NAMES = {1: "INVALID_ARG", 2: "UNSUPPORTED", 3: "ALIGNMENT", 4: "LAUNCH", 5: "OVERFLOW",
              6: "DEVICE"}
@@ -186,33 +181,12 @@ def arm_stall(kernel: int, wait_limit_cycles: int) -> None:
 
 
 def zero_gemv_workspaces() -> None:
-    """Zeroes every streaming-GEMV and decode-chain workspace of this process (needed after
-    a launch that unwound on a wait timeout: its counters may be left non-zero)."""
-    for buf in list(_workspaces.values()) + list(_chain_workspaces.values()):
+    """Zeroes every streaming-GEMV workspace of this process (needed after a launch that
+    unwound on a wait timeout: its row-block counters may be left non-zero)."""
+    for buf in _workspaces.values():
         buf.zero_()
-    for dev_idx in set(_workspaces) | set(_chain_workspaces):
+    for dev_idx in _workspaces:
         torch.cuda.synchronize(dev_idx)
-
-
-_chain_workspaces: dict[int, torch.Tensor] = {}
-
-
-def chain_workspace(device: torch.device) -> tuple[int | None, int]:
-    """(pointer, bytes) of the decode-chain workspace of `device`: one zero-filled buffer
-    per device for the life of the process (captured graphs hold its address); the kernel
-    leaves it zeroed after every call. None while a capture is running and no buffer
-    exists yet (the caller then keeps its unfused path)."""
-    _ensure_device(device)
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    buf = _chain_workspaces.get(idx)
-    if buf is None:
-        if torch.cuda.is_current_stream_capturing():
-            return None, 0
-        need = int(lib().umic_decode_chain_workspace_bytes())
-        buf = torch.zeros(need, dtype=torch.uint8, device=device)
-        torch.cuda.current_stream(device).synchronize()
-        _chain_workspaces[idx] = buf
-    return buf.data_ptr(), buf.numel()
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -316,7 +316,6 @@ def has_axpy_epilogue(norm: nn.Module | None) -> bool:
 @dataclass(frozen=True)
 class LayerSite:
     post_norm: nn.Module
-    decode_chain: bool = True  # decode rows run the one-launch MLP chain
 
 
 def _match_decoder_layer(module: nn.Module) -> LayerSite | None:
@@ -331,73 +330,26 @@ def _decoder_layer_forward(self: nn.Module, hidden_states: torch.Tensor,
     """stream -> norm -> attention; the attention residual add runs inside the
     post-attention RMSNorm (one kernel, two outputs: the MLP input and the new
     stream); the MLP residual add runs in the down projection's epilogue when the MLP
-    is a rebound SwiGLU block (the reference kept both adds eager, integrate.py:180-209).
-    Decode rows (one token per episode) with a rebound attention and MLP take the decode
-    chain instead: o_proj, the add+RMSNorm and the whole MLP as one persistent kernel."""
+    is a rebound SwiGLU block (the reference kept both adds eager, integrate.py:180-209)."""
     site: LayerSite = self.__dict__[_SITE]
-    attn_in = self.input_layernorm(hidden_states)
-    mlp_site = _site(self.mlp, SwiGLUSite)
-    if site.decode_chain and mlp_site is not None and hidden_states.shape[-2] * \
-            math.prod(hidden_states.shape[:-2]) <= DECODE_CHAIN_MAX_ROWS:
-        out = _decode_chain_layer(self, site, mlp_site, hidden_states, attn_in,
-                                  position_embeddings, kwargs)
-        if out is not None:
-            return out
-    attn_out = self.self_attn(hidden_states=attn_in, position_embeddings=position_embeddings,
-                              **kwargs)[0]
+    attn_out = self.self_attn(hidden_states=self.input_layernorm(hidden_states),
+                              position_embeddings=position_embeddings, **kwargs)[0]
     mlp_in, stream = add_rmsnorm(attn_out, hidden_states, site.post_norm.weight,
                                  _eps_of(site.post_norm))
+    mlp_site = _site(self.mlp, SwiGLUSite)
     if mlp_site is not None:
         return swiglu(mlp_site, mlp_in, residual=stream)
     return stream + self.mlp(mlp_in)
-
-
-# Rows up to which a decoder layer's decode step runs the decode chain kernel.
-DECODE_CHAIN_MAX_ROWS = 16
-
-
-def _decode_chain_layer(layer, site, mlp_site, hidden_states, attn_in, position_embeddings,
-                        kwargs):
-    """The decode chain: attention up to (not including) o_proj on the fused attention
-    path, then o_proj + add + RMSNorm + gate/up + down + residual in one launch. None
-    (before anything ran) when the attention or the chain kernel does not cover the call."""
-    from .kernels.decode import decode_mlp_chain
-
-    attn = layer.self_attn
-    o_proj = getattr(attn, "o_proj", None)
-    if (not isinstance(o_proj, nn.Linear) or o_proj.bias is not None
-            or attn.__dict__.get("forward") is None
-            or attn.forward.__func__ is not _qk_attention_forward
-            or not _kernel_covers(attn, attn_in, (position_embeddings or (None,))[0])):
-        return None
-    core = _qk_attention_core(attn, attn_in, position_embeddings,
-                              kwargs.get("attention_mask"), kwargs.get("past_key_values"),
-                              {k: v for k, v in kwargs.items()
-                               if k not in ("attention_mask", "past_key_values")})
-    pre_o = core[0].reshape(-1, core[0].shape[-1])
-    h2d = hidden_states.reshape(-1, hidden_states.shape[-1])
-    post = site.post_norm
-    out = decode_mlp_chain(pre_o, o_proj.weight, h2d, post.weight, _eps_of(post),
-                           mlp_site.gate.weight, mlp_site.up.weight, mlp_site.down.weight)
-    if out is None:  # the attention ran already: finish on the unfused kernels
-        attn_out = _project_rows(o_proj, pre_o)
-        mlp_in, stream = add_rmsnorm(attn_out, h2d, post.weight, _eps_of(post))
-        out = swiglu(mlp_site, mlp_in, residual=stream)
-    return out.view(hidden_states.shape)
 
 
 DECODER_LAYER = Motif("decoder layer (add+RMSNorm residual fold)", _match_decoder_layer,
                       _decoder_layer_forward)
 
 
-def fuse_add_rmsnorm(model: nn.Module, dry_run: bool = False, decode_chain: bool = True) -> int:
+def fuse_add_rmsnorm(model: nn.Module, dry_run: bool = False) -> int:
     """Fold the decoder layers' residual adds into kernels that already read the
-    operands (src/umic/integrate.py:212-231); with `decode_chain`, decode rows run the
-    layer's o_proj + add+RMSNorm + MLP as one launch."""
-    def install(module, site):
-        _install(module, _decoder_layer_forward, LayerSite(site.post_norm, decode_chain))
-
-    return _rebind(model, DECODER_LAYER, dry_run, install)
+    operands (src/umic/integrate.py:212-231)."""
+    return _rebind(model, DECODER_LAYER, dry_run)
 
 
 # ============================================ text attention input path (f2)

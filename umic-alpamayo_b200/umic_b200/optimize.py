@@ -11,8 +11,6 @@ Additions, on by default and reported:
   * vision_gemm_fusion: the ViT MLPs run fc1 with the tanh-GELU in the GEMM
     epilogue (the reference's epilogue was erf-only, so it kept them on cuBLAS), and
     the ViT attention's qkv projection runs on the same GEMM;
-  * decode_chain: for decode rows (one token per episode) a decoder layer's o_proj,
-    post-attention add+RMSNorm and whole MLP run as one persistent kernel;
   * the expert's MLPs and q/o projections take the same GEMMs as the LM;
   * the LM / expert lookups also accept the transformers 5.x layout, where the
     VLM holds its language model and vision tower under `.model`.
@@ -47,7 +45,6 @@ class UmicConfig:
     decode_gemv: bool = True
     attention_fusion: bool = True
     vision_gemm_fusion: bool = True
-    decode_chain: bool = True
 
 
 # Where the LM trunk may sit under model.vlm, in lookup order: (module to return, module
@@ -101,8 +98,7 @@ def _lm_phase(lm: nn.Module, cfg: UmicConfig, report: dict, prefix: str) -> None
         (cfg.mlp_fusion, "mlp", integrate.fuse_mlps),
         (cfg.linear_fusion, "linear", integrate.fuse_linears),
         (cfg.norm_fusion, "rmsnorm", integrate.fuse_rmsnorms),
-        (cfg.add_rmsnorm_fusion, "add_rmsnorm",
-         lambda m: integrate.fuse_add_rmsnorm(m, decode_chain=cfg.decode_chain)),
+        (cfg.add_rmsnorm_fusion, "add_rmsnorm", integrate.fuse_add_rmsnorm),
         (cfg.attention_fusion, "attention", integrate.fuse_attention),
     )
     for enabled, what, fuse in steps:
@@ -148,8 +144,7 @@ def _expert_phase(expert: nn.Module, cfg: UmicConfig, report: dict) -> None:
         if cfg.norm_fusion:
             report["expert_rmsnorm_fused"] = integrate.fuse_rmsnorms(expert)
         if cfg.add_rmsnorm_fusion:
-            report["expert_add_rmsnorm_fused"] = integrate.fuse_add_rmsnorm(
-                expert, decode_chain=cfg.decode_chain)
+            report["expert_add_rmsnorm_fused"] = integrate.fuse_add_rmsnorm(expert)
 
 
 def _decode_phase(model: nn.Module, lm, expert, cfg: UmicConfig, report: dict) -> None:
