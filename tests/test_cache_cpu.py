@@ -124,3 +124,26 @@ def test_repeat_cache_hook_converts_once_and_resyncs(fake_kernel):
     seen[0].layers[0].update(torch.zeros(2, 3, 2, 8), torch.zeros(2, 3, 2, 8))
     ex(inputs_embeds=emb, past_key_values=dyn)  # re-sync: crop back to the caller's length
     assert seen[2].get_seq_length() == 5
+
+
+def test_fuse_flow_graph_wraps_the_sampler_step_callables():
+    """The reference's fuse_flow_graph contract: sample() receives its step callables
+    wrapped in FlowStepGraph; the first `warmup` calls of a step run eagerly (no CUDA)."""
+    from types import SimpleNamespace
+
+    from umic_b200.graph import FlowStepGraph, fuse_flow_graph
+
+    seen = {}
+
+    def sample(x, step_fn=None, unguided_step_fn=None):
+        seen["step"], seen["unguided"] = step_fn, unguided_step_fn
+        t = torch.zeros(1)
+        for _ in range(2):
+            x = step_fn(x=x, t=t)
+        return x
+
+    model = SimpleNamespace(diffusion=SimpleNamespace(sample=sample))
+    fuse_flow_graph(model, warmup=2)
+    out = model.diffusion.sample(torch.ones(3), step_fn=lambda x, t: x * 2)
+    assert isinstance(seen["step"], FlowStepGraph) and seen["unguided"] is None
+    assert torch.equal(out, torch.full((3,), 4.0)) and seen["step"].graph is None

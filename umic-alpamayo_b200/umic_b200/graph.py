@@ -322,3 +322,22 @@ class FlowStepGraph:
         self.inputs[0].copy_(x)
         self.inputs[1].copy_(t)
         return self.bank.run(0, self._captured_step).clone()
+
+
+def fuse_flow_graph(model: torch.nn.Module, warmup: int = 2) -> None:
+    """Replay every ODE step of `model.diffusion.sample` from a CUDA graph
+    (src/umic/graph.py:235-253): the step callables the model hands to its sampler
+    (`step_fn`, `unguided_step_fn`) are wrapped in FlowStepGraph for the duration of each
+    sample() call; the sampler itself is untouched."""
+    sampler = model.diffusion
+    inner = sampler.sample
+
+    def sample_with_step_graphs(*args: Any, **kwargs: Any):
+        for key in ("step_fn", "unguided_step_fn"):
+            if kwargs.get(key) is not None:
+                kwargs[key] = FlowStepGraph(kwargs[key], warmup)
+        return inner(*args, **kwargs)
+
+    sampler.sample = sample_with_step_graphs
+    logger.info("fuse_flow_graph: ODE steps of %s.sample replay from CUDA graphs",
+                type(sampler).__name__)
