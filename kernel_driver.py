@@ -9,6 +9,7 @@ Used to capture a single kernel under ncu. Modes and shapes:
   qk_prep        q/k RMSNorm + RoPE + K/V cache write, [rows=8 episodes, 3100, 32/8, 128]
   add_rmsnorm    [3100, 4096]                  (cfg2a)
   add_layernorm  [16384, 1280]                 (cfg2b)
+  rmsnorm_axpy   x + dt * rmsnorm(h) in place, [rows=2048, 2048] (cfg5 Euler update)
   rope_text      q [3100, 32, 128], k [3100, 8, 128], bf16 tables   (cfg2c)
   rope_vision    q, k [16384, 16, 80] views of qkv, fp32 tables     (cfg2d)
   gemv           x [rows=8, 4096], W [12288, 4096]
@@ -80,6 +81,13 @@ def make(mode: str, rows: int | None):
         r = torch.randn_like(x)
         w = torch.randn(4096, device=dev, dtype=bf)
         return lambda: add_rmsnorm(x, r, w, 1e-6)
+    if mode == "rmsnorm_axpy":  # the flow Euler update at the cfg5 shape (32 x 64 tokens)
+        from umic_b200.kernels import rmsnorm_axpy
+
+        h = torch.randn(rows or 2048, 2048, device=dev, dtype=bf)
+        x = torch.randn_like(h)
+        w = torch.ones(2048, device=dev, dtype=bf)
+        return lambda: rmsnorm_axpy(h, w, 1e-6, x, 0.1, out=x)
     if mode == "add_layernorm":
         x = torch.randn(16384, 1280, device=dev, dtype=bf)
         r = torch.randn_like(x)
