@@ -327,6 +327,26 @@ UMIC_API int umic_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, c
               const void* residual, int64_t ldr, void* y, int64_t ldy, int64_t m,
               int64_t n, int64_t k, int epilogue, void* stream);
 
+/* umic_gemm with a caller workspace that enables split-K for shapes whose output tiles
+ * would leave most of the GPU idle (at most half the CTA pairs busy: e.g. the flow
+ * expert's q/o/down projections over 4 episodes, 256 rows x 2048 columns = 8 tiles for
+ * 74 CTA pairs). Each tile's k-blocks are then cut into up to 16 ranges, one work unit
+ * each; a unit writes its fp32 partial to the workspace and the last unit of a tile half
+ * sums the partials in range order (deterministic) and runs the epilogue (bias, GELU,
+ * residual). Other shapes run exactly as umic_gemm. workspace: at least
+ * umic_gemm_workspace_bytes(m, n, k) bytes (0 when no split applies), 256-byte aligned,
+ * zero-filled before its first use; every call leaves its counters at zero. Calls sharing
+ * a workspace must be ordered on one stream. Replaces linear_triton (linear.py:118-145)
+ * for the small-row shapes the reference sent to cuBLAS. */
+UMIC_API int umic_gemm_ws(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                          const void* bias, const void* residual, int64_t ldr, void* y,
+                          int64_t ldy, int64_t m, int64_t n, int64_t k, int epilogue,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace umic_gemm_ws needs for this shape on the current device (0: the
+ * shape fills the GPU without splitting). */
+UMIC_API size_t umic_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k);
+
 /* Dual-accumulator tensor-core GEMM with the SwiGLU epilogue in registers:
  * h = silu(x . wg^T) * (x . wu^T); the gate and up products never reach HBM.
  * wg / wu are [n, k] (nn.Linear layout). Same alignment rules as umic_gemm.

@@ -130,3 +130,14 @@ def test_debug_stall_rejects_bad_arguments():
     assert L.umic_debug_stall(0, 1000) == 1
     assert L.umic_debug_stall(1, 0) == 1
     assert "umic_debug_stall" in _lib.last_message()
+
+
+def test_gemm_split_plan_on_host():
+    """Split-K only for shapes whose tiles fill at most half the CTA pairs: the flow
+    expert's projections at 4 episodes get a workspace, the LM prefill shapes none."""
+    L = _lib.lib()
+    assert L.umic_gemm_workspace_bytes(256, 2048, 2048) > 0
+    assert L.umic_gemm_workspace_bytes(256, 2048, 8192) > 0
+    assert L.umic_gemm_workspace_bytes(24800, 4096, 4096) == 0
+    assert L.umic_gemm_workspace_bytes(3100, 4096, 4096) == 0
+    assert L.umic_gemm_workspace_bytes(256, 2048, 256) == 0  # too few k-blocks to split

@@ -447,6 +447,36 @@ def test_gemm(cuda, m, n, k):
     y = linear(x, w)
     assert stats["umic_gemm"] == 1 and stats["linear_fallback"] == 0
     _close(y, _gpu_ref_linear(x, w))
+    # the first and last row blocks also against the CPU oracle (fp32 restatement)
+    for rows in (slice(0, 64), slice(max(0, m - 64), m)):
+        _close(y[rows], oracle.linear(x[rows].cpu(), w.cpu()))
+
+
+@pytest.mark.parametrize("m,n,k,act,res", [
+    (256, 2048, 2048, None, False),       # the flow expert's q/o at 4 episodes: 8 tiles
+    (256, 2048, 8192, None, True),        # its down_proj, residual in the epilogue
+    (512, 1024, 4096, "gelu_tanh", False),  # bias + GELU after the split sum
+    (100, 2048, 2048, None, False),       # single-CTA tiles
+    (300, 520, 1000, None, True),         # ragged rows, columns and k
+])
+def test_gemm_split_k(cuda, m, n, k, act, res):
+    """Under-filled tile grids run split-K (fp32 partials summed in range order by the
+    last unit of each tile half): against fp32, against the unsplit kernel, and
+    deterministic from call to call."""
+    x = _randn(m, k, seed=70, dev=cuda)
+    w = _randn(n, k, seed=71, dev=cuda, scale=0.02)
+    b = _randn(n, seed=72, dev=cuda) if act else None
+    r = _randn(m, n, seed=73, dev=cuda) if res else None
+    assert _lib.lib().umic_gemm_workspace_bytes(m, n, k) > 0
+    stats.clear()
+    y = linear(x, w, b, act=act, residual=r)
+    assert stats["umic_gemm_split_k"] == 1
+    _close(y, _gpu_ref_linear(x, w, b, act, r))
+    _close(y[:64], oracle.linear(x[:64].cpu(), w.cpu(), None if b is None else b.cpu(), act,
+                                 None if r is None else r[:64].cpu()))
+    y1 = linear(x, w, b, act=act, residual=r, split_k=False)
+    assert oracle.rel_err(y, y1) <= 2e-3  # the same sums in another order
+    assert torch.equal(y, linear(x, w, b, act=act, residual=r))
 
 
 def test_gemm_small_vs_cpu_oracle(cuda):

@@ -255,6 +255,7 @@ def test_flow_expert_euler(cuda):
     assert stats["umic_qk_norm_rope_kv"] == 18 * 10  # KV write fused into the attention prep
     assert stats["umic_attention_rows"] == 18 * 10  # masked prefix attention on tcgen05
     assert stats["umic_rmsnorm_axpy"] == 10  # x + dt * v inside the expert's final norm
+    assert stats["umic_mask_pack_bits"] == 10  # the step's mask packed once, not per layer
     # the same 10 steps with one captured Euler step replayed: 2 eager warm-up steps, one
     # side-stream pass before capture and the capture itself go through Python; the 8
     # replays launch the same kernels from the graph

@@ -86,6 +86,12 @@ struct TcParams {
   int epilogue;
   long long wait_limit;  // SM cycles a bounded wait may take before the CTA unwinds
   int stall;             // test hook: CTA 0 skips the loads of its first stage
+  // Split-K (linear only): each tile's k-blocks are cut into `splits` contiguous ranges,
+  // one work unit each; a unit writes its fp32 partial to `part` and the last of a tile
+  // half's units (counted in `cnt`) sums them in split order and runs the epilogue.
+  int splits;
+  float* part;    // [tiles][2 halves][splits][128 rows][kBN cols]
+  unsigned* cnt;  // [tiles][2 halves], zero between calls
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -242,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // bars: full[kStages], empty[kStages], acc_full[2], acc_empty[2], drain
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * G::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;  // split-K: this CTA sums the tile half
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = kPair == 2 ? cluster_rank() : 0;  // position in the CTA pair
@@ -251,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t drain = accf0 + 32;
   const uint32_t sbase = smem_u32(smem);
   const int tiles = p.tiles_m * p.tiles_n;
+  const int work = tiles * p.splits;  // work units: (tile, k range)
   const int unit = kPair == 2 ? static_cast<int>(blockIdx.x) / 2 : static_cast<int>(blockIdx.x);
   const int units = kPair == 2 ? static_cast<int>(gridDim.x) / 2 : static_cast<int>(gridDim.x);
 
@@ -299,7 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued = false;
-      for (int t = unit; t < tiles && ok; t += units) {
+      for (int w = unit; w < work && ok; w += units) {
+        const int t = w / p.splits, sp = w - t * p.splits;
+        const int kb0 = sp * p.kblocks / p.splits, kb1 = (sp + 1) * p.kblocks / p.splits;
         int mb, nb;
         tile_coords(t, p, mb, nb);
         const int row_a = mb * G::kTileM + static_cast<int>(rank) * kBM;
@@ -311,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           row_b = nb * kBN + static_cast<int>(rank) * (kBN / kPair);
         }
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.err, abort_flag, p.wait_limit)) {
             ok = false;
             break;
@@ -375,7 +385,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       const uint32_t peer = kPair == 2 ? 1u : 0u;
-      for (int t = unit; t < tiles && ok; t += units, ++it) {
+      for (int w = unit; w < work && ok; w += units, ++it) {
+        const int t = w / p.splits, sp = w - t * p.splits;
+        const int kb0 = sp * p.kblocks / p.splits, kb1 = (sp + 1) * p.kblocks / p.splits;
+        (void)t;
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, p.err, abort_flag, p.wait_limit)) {
@@ -384,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * kBN;
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(full0 + 8 * stage, phase, p.err, abort_flag, p.wait_limit)) {
             ok = false;
             break;
@@ -395,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             // +32 bytes along K inside the swizzle atom = +2 in the >>4 field
-            mma_bf16<kPair>(tmem_d, ad + 2 * kk, bd + 2 * kk, (kb | kk) ? 1u : 0u);
+            mma_bf16<kPair>(tmem_d, ad + 2 * kk, bd + 2 * kk, ((kb - kb0) | kk) ? 1u : 0u);
           }
           mma_commit<kPair>(empty0 + 8 * stage);  // frees this stage in both CTAs
           if (kPair == 2) mma_commit<kPair>(cluster_addr(empty0 + 8 * stage, peer));
@@ -421,17 +434,77 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stg0 = sbase + G::kStageOut + quarter * 4096;
     int chunk_idx = 0;
     int it = 0;
-    for (int t = unit; t < tiles; t += units, ++it) {
+    constexpr int kOutCols = kDual ? kBN / 2 : kBN;
+    const int erow = quarter * 32 + lane;  // this thread's accumulator row (TMEM lane)
+    // Bias / activation / residual on one 32-column chunk of this thread's row, then the
+    // warp's 32 x 32 chunk staged in shared memory (64-byte swizzle: 16-byte chunk j of
+    // row r at j ^ ((r >> 1) & 3), conflict-free) and written with one TMA store.
+    auto store_chunk = [&](float (&v)[32], int mb, int cbase) {
+      const int row = mb * G::kTileM + static_cast<int>(rank) * kBM + erow;
+      const bool live = row < p.m;  // rows past m hold zeros; the TMA store clips them
+      if (!kDual) {
+        if (p.bias) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            if (cbase + i < p.n) {
+              float b[8];
+              unpack8(ld_cached(p.bias + cbase + i), b);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i + j] += b[j];
+            }
+          }
+        }
+        if (p.epilogue == UMIC_EPI_GELU_ERF) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+        } else if (p.epilogue == UMIC_EPI_GELU_TANH) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+        }
+        if (p.residual && live) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            if (cbase + i < p.n) {
+              float r[8];
+              unpack8(ld_stream(p.residual + static_cast<int64_t>(row) * p.ldr + cbase + i), r);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i + j] += r[j];
+            }
+          }
+        }
+      }
+      const uint32_t buf = stg0 + (chunk_idx & 1) * 2048;
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float o[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) o[jj] = v[j * 8 + jj];
+        st_shared_v4(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4), pack8(o));
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&map_y, buf, cbase,
+                     mb * G::kTileM + static_cast<int>(rank) * kBM + quarter * 32);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+      ++chunk_idx;
+    };
+    for (int w = unit; w < work; w += units, ++it) {
+      const int t = w / p.splits, sp = w - t * p.splits;
       int mb, nb;
       tile_coords(t, p, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(accf0 + 8 * acc, acc_phase, p.err, abort_flag, p.wait_limit)) break;
       tc_fence_after();
-      const int row = mb * G::kTileM + static_cast<int>(rank) * kBM + quarter * 32 + lane;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
-      constexpr int kOutCols = kDual ? kBN / 2 : kBN;
       const int col0 = nb * kOutCols;
+      // split-K: this unit's fp32 partial rows [128][kOutCols] of the tile half
+      float* part_base = p.part + (static_cast<size_t>(t) * 2 + rank) * p.splits *
+                                      (static_cast<size_t>(kBM) * kOutCols);
 #pragma unroll 1
       for (int c = 0; c < kOutCols; c += 32) {
         __syncwarp();  // tcgen05.ld is warp-collective
@@ -449,59 +522,57 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (kPair == 2) mbar_arrive_cluster(lead_acce0 + 8 * acc);
           else mbar_arrive(acce0 + 8 * acc);
         }
-        const bool live = row < p.m;  // rows past m hold zeros; the TMA store clips them
-        const int cbase = col0 + c;
-        if (!kDual) {
-          if (p.bias) {
+        if (p.splits == 1) {
+          store_chunk(v, mb, col0 + c);
+        } else {
+          float4* dst = reinterpret_cast<float4*>(
+              part_base + static_cast<size_t>(sp) * kBM * kOutCols +
+              static_cast<size_t>(erow) * kOutCols + c);
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              if (cbase + i < p.n) {
-                float b[8];
-                unpack8(ld_cached(p.bias + cbase + i), b);
+          for (int i = 0; i < 8; ++i)
+            __stcg(dst + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+        }
+      }
+      if (p.splits > 1) {
+        // count this unit in; the last unit of the tile half sums the partials in split
+        // order (deterministic whatever the arrival order) and runs the epilogue
+        __threadfence();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (quarter == 0 && lane == 0) {
+          unsigned prev;
+          asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                       : "=r"(prev)
+                       : "l"(p.cnt + static_cast<size_t>(t) * 2 + rank)
+                       : "memory");
+          *last_flag = prev == static_cast<unsigned>(p.splits - 1);
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (*last_flag) {
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+#pragma unroll 1
+          for (int c = 0; c < kOutCols; c += 32) {
+            float v[32];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[i + j] += b[j];
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+#pragma unroll 1
+            for (int j = 0; j < p.splits; ++j) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  part_base + static_cast<size_t>(j) * kBM * kOutCols +
+                  static_cast<size_t>(erow) * kOutCols + c);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 q = __ldcg(src + i);
+                v[4 * i] += q.x;
+                v[4 * i + 1] += q.y;
+                v[4 * i + 2] += q.z;
+                v[4 * i + 3] += q.w;
               }
             }
+            store_chunk(v, mb, col0 + c);
           }
-          if (p.epilogue == UMIC_EPI_GELU_ERF) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-          } else if (p.epilogue == UMIC_EPI_GELU_TANH) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
-          }
-          if (p.residual && live) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              if (cbase + i < p.n) {
-                float r[8];
-                unpack8(ld_stream(p.residual + static_cast<int64_t>(row) * p.ldr + cbase + i), r);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[i + j] += r[j];
-              }
-            }
-          }
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          if (quarter == 0 && lane == 0) p.cnt[static_cast<size_t>(t) * 2 + rank] = 0;
         }
-        // Stage the warp's 32 x 32 chunk (64-byte swizzle: 16-byte chunk j of row r at
-        // j ^ ((r >> 1) & 3), conflict-free) and store it with one TMA copy.
-        const uint32_t buf = stg0 + (chunk_idx & 1) * 2048;
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float o[8];
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) o[jj] = v[j * 8 + jj];
-          st_shared_v4(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4), pack8(o));
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&map_y, buf, cbase,
-                       mb * G::kTileM + static_cast<int>(rank) * kBM + quarter * 32);
-          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        }
-        ++chunk_idx;
       }
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -552,10 +623,42 @@ int check_operand(const char* name, const char* what, const void* p, int64_t ld,
   return UMIC_OK;
 }
 
+// Split-K plan of a linear launch: when the output tiles would fill at most half of the
+// CTA pairs (or single CTAs), each tile's k-blocks are cut into `splits` ranges so the work
+// units fill the GPU (at least 4 k-blocks per range, at most 16 ranges). 1 = no split.
+struct SplitPlan {
+  int splits = 1;
+  size_t part_bytes = 0, cnt_offset = 0, bytes = 0;
+};
+
+SplitPlan plan_split(int64_t m, int64_t n, int64_t k, int units_max) {
+  SplitPlan sp;
+  const bool pair = m > kBM;
+  const int64_t tiles = ((m + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM)) *
+                        ((n + kBN - 1) / kBN);
+  const int64_t kblocks = (k + kBK - 1) / kBK;
+  if (tiles <= 0 || tiles * 2 > units_max || kblocks < 8) return sp;
+  int64_t s = units_max / tiles;
+  if (s > kblocks / 4) s = kblocks / 4;
+  if (s > 16) s = 16;
+  if (s < 2) return sp;
+  sp.splits = static_cast<int>(s);
+  sp.part_bytes = static_cast<size_t>(tiles) * 2 * s * kBM * kBN * sizeof(float);
+  sp.cnt_offset = (sp.part_bytes + 255) & ~static_cast<size_t>(255);
+  sp.bytes = sp.cnt_offset + ((static_cast<size_t>(tiles) * 2 * 4 + 255) & ~static_cast<size_t>(255));
+  return sp;
+}
+
+int units_for(int64_t m) {
+  const int sms = sm_count();
+  return m > kBM ? sms / 2 : sms;
+}
+
 template <bool kDual>
 int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw,
         const void* w2, int64_t ldw2, const void* bias, const void* residual, int64_t ldr,
-        void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, int epilogue, void* stream) {
+        void* y, int64_t ldy, int64_t m, int64_t n, int64_t k, int epilogue, void* stream,
+        void* workspace = nullptr, size_t workspace_bytes = 0) {
   clear_error();
   if (m < 0 || n < 0 || k <= 0) return fail(UMIC_ERR_INVALID_ARG, "%s: bad sizes", name);
   if (m == 0 || n == 0) return UMIC_OK;
@@ -603,6 +706,20 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   p.tiles_n = static_cast<int>((n + out_cols - 1) / out_cols);
   p.kblocks = static_cast<int>((k + kBK - 1) / kBK);
   p.epilogue = epilogue;
+  p.splits = 1;
+  p.part = nullptr;
+  p.cnt = nullptr;
+  if (!kDual && workspace) {
+    const SplitPlan sp = plan_split(m, n, k, units_for(m));
+    if (sp.splits > 1) {
+      if (workspace_bytes < sp.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return fail(UMIC_ERR_INVALID_ARG, "%s: workspace of %zu bytes (256-byte aligned) "
+                    "needed, %zu given", name, sp.bytes, workspace_bytes);
+      p.splits = sp.splits;
+      p.part = static_cast<float*>(workspace);
+      p.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) + sp.cnt_offset);
+    }
+  }
   p.wait_limit = kWaitLimitCycles;
   p.stall = 0;
   {
@@ -612,7 +729,7 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
       p.wait_limit = limit;
     }
   }
-  const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n * p.splits;  // work units
   if (tiles > 0x7fffffffLL) return fail(UMIC_ERR_UNSUPPORTED, "%s: too many tiles", name);
   const int sms = sm_count();
   cudaStream_t st = as_stream(stream);
@@ -653,6 +770,19 @@ int umic_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void
               int64_t k, int epilogue, void* stream) {
   return run<false>("umic_gemm", x, ldx, w, ldw, nullptr, 0, bias, residual, ldr, y, ldy, m, n, k,
                     epilogue, stream);
+}
+
+int umic_gemm_ws(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+                 const void* residual, int64_t ldr, void* y, int64_t ldy, int64_t m, int64_t n,
+                 int64_t k, int epilogue, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  return run<false>("umic_gemm_ws", x, ldx, w, ldw, nullptr, 0, bias, residual, ldr, y, ldy, m,
+                    n, k, epilogue, stream, workspace, workspace_bytes);
+}
+
+size_t umic_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  return plan_split(m, n, k, units_for(m)).bytes;
 }
 
 int umic_gemm_gate_silu_mul(const void* x, int64_t ldx, const void* wg, int64_t ldwg,

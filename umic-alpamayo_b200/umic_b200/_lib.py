@@ -71,10 +71,14 @@ _SIGNATURES: dict[str, list] = {
                             _c_i64, _c_i64, _c_i64, _c_p],
     "umic_gemm": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64,
                   _c_i64, _c_int, _c_p],
+    "umic_gemm_ws": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i64,
+                     _c_i64, _c_i64, _c_int, _c_p, _c_size, _c_p],
+    "umic_gemm_workspace_bytes": [_c_i64, _c_i64, _c_i64],
     "umic_gemm_gate_silu_mul": [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_i64,
                                 _c_i64, _c_i64, _c_p],
 }
-_RESTYPES = {"umic_last_error_message": ctypes.c_char_p, "umic_gemv_workspace_bytes": _c_size}
+_RESTYPES = {"umic_last_error_message": ctypes.c_char_p, "umic_gemv_workspace_bytes": _c_size,
+             "umic_gemm_workspace_bytes": _c_size}
 
 ERR_NAMES = {1: "INVALID_ARG", 2: "UNSUPPORTED", 3: "ALIGNMENT", 4: "LAUNCH", 5: "OVERFLOW",
              6: "DEVICE"}
@@ -181,12 +185,38 @@ def arm_stall(kernel: int, wait_limit_cycles: int) -> None:
 
 
 def zero_gemv_workspaces() -> None:
-    """Zeroes every streaming-GEMV workspace of this process (needed after a launch that
-    unwound on a wait timeout: its row-block counters may be left non-zero)."""
-    for buf in _workspaces.values():
+    """Zeroes every streaming-GEMV and split-K GEMM workspace of this process (needed after
+    a launch that unwound on a wait timeout: its counters may be left non-zero)."""
+    for buf in list(_workspaces.values()) + list(_gemm_workspaces.values()):
         buf.zero_()
-    for dev_idx in _workspaces:
+    for dev_idx in set(_workspaces) | set(_gemm_workspaces):
         torch.cuda.synchronize(dev_idx)
+
+
+_gemm_workspaces: dict[int, torch.Tensor] = {}
+
+
+def gemm_workspace(device: torch.device, m: int, n: int, k: int) -> tuple[int | None, int]:
+    """(pointer, bytes) of the split-K GEMM workspace of `device` for this shape, or
+    (None, 0) when the shape needs no split. One zero-filled buffer per device for the
+    process (captured graphs hold its address; an outgrown buffer is retired, never freed);
+    the kernel returns its counters to zero after every call. While a capture runs and the
+    buffer is too small, (None, 0): the call then runs without splitting."""
+    _ensure_device(device)
+    need = int(lib().umic_gemm_workspace_bytes(m, n, k))
+    if need == 0:
+        return None, 0
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _gemm_workspaces.get(idx)
+    if buf is None or buf.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            return None, 0
+        if buf is not None:
+            _retired.append(buf)
+        buf = torch.zeros(need, dtype=torch.uint8, device=device)
+        torch.cuda.current_stream(device).synchronize()
+        _gemm_workspaces[idx] = buf
+    return buf.data_ptr(), buf.numel()
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -72,6 +72,35 @@ def qk_norm_rope_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor | None,
     stats["umic_qk_norm_rope_kv"] += 1
 
 
+# The packed form of the last mask seen. Every layer of a model's forward receives the
+# same boolean mask (transformers builds it once per forward), so it is packed once and
+# reused by the other layers. The key holds the mask's base tensor by weak reference
+# (alive tensors cannot share memory, so a reused address never matches a dead mask),
+# the view's geometry and the version counter (an in-place write invalidates it).
+_mask_cache: dict = {"base": None, "key": None, "bits": None}
+
+
+def _packed_mask(mask: torch.Tensor, lk: int, dev: torch.device) -> torch.Tensor:
+    import weakref
+
+    base = mask if mask._base is None else mask._base
+    key = (mask.data_ptr(), tuple(mask.shape), tuple(mask.stride()), mask._version, lk,
+           torch.cuda.is_current_stream_capturing())
+    ref = _mask_cache["base"]
+    if ref is not None and ref() is base and _mask_cache["key"] == key:
+        stats["mask_bits_reused"] += 1
+        return _mask_cache["bits"]
+    src = mask if mask.stride(-1) == 1 else mask.contiguous()
+    hm, words = src.shape[1], (lk + 31) // 32
+    bits = torch.empty(src.shape[0], hm, src.shape[2], words, device=dev, dtype=torch.int32)
+    _lib.call("umic_mask_pack_bits", dev, src.data_ptr(), src.stride(0), src.stride(1),
+              src.stride(2), src.shape[0], hm, src.shape[2], lk, bits.data_ptr(),
+              bits.stride(0), bits.stride(1), bits.stride(2))
+    stats["umic_mask_pack_bits"] += 1
+    _mask_cache.update(base=weakref.ref(base), key=key, bits=bits)
+    return bits
+
+
 def attention_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                    mask: torch.Tensor | None, scale: float) -> torch.Tensor | None:
     """softmax(scale * q k^T, masked) v with grouped-query heads, on the tcgen05 kernel.
@@ -100,15 +129,8 @@ def attention_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         if mask.shape[1] not in (1, hq) or mask.shape[0] not in (1, bsz) or \
                 mask.shape[2] not in (1, t):
             return None
-        if mask.stride(-1) != 1:
-            mask = mask.contiguous()
-        hm, words = mask.shape[1], (lk + 31) // 32
-        bits = torch.empty(mask.shape[0], hm, mask.shape[2], words, device=dev,
-                           dtype=torch.int32)
-        _lib.call("umic_mask_pack_bits", dev, mask.data_ptr(), mask.stride(0),
-                  mask.stride(1), mask.stride(2), mask.shape[0], hm, mask.shape[2], lk,
-                  bits.data_ptr(), bits.stride(0), bits.stride(1), bits.stride(2))
-        stats["umic_mask_pack_bits"] += 1
+        bits = _packed_mask(mask, lk, dev)
+        hm = bits.shape[1]
         ws = (bits.stride(0) if bits.shape[0] > 1 else 0, bits.stride(1) if hm > 1 else 0,
               bits.stride(2) if bits.shape[2] > 1 else 0)
     out = torch.empty(bsz, t, hq, d, device=dev, dtype=q.dtype)

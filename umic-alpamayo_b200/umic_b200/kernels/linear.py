@@ -42,8 +42,11 @@ def _k_major(t: torch.Tensor) -> torch.Tensor:
 
 
 def linear(x2d: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
-           act: str | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
-    """y = act(x2d @ weight.T + bias) + residual on the tcgen05 GEMM."""
+           act: str | None = None, residual: torch.Tensor | None = None,
+           split_k: bool = True) -> torch.Tensor:
+    """y = act(x2d @ weight.T + bias) + residual on the tcgen05 GEMM. Shapes whose output
+    tiles would leave most of the GPU idle run split-K through a per-device workspace
+    (umic_gemm_ws) unless split_k is False."""
     if act not in _ACTS:
         raise ValueError(f"linear: unsupported act {act!r}")
     dev = require_cuda("linear", x2d, weight, bias, residual)
@@ -57,10 +60,16 @@ def linear(x2d: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = 
     y = torch.empty((m, n), device=x2d.device, dtype=x2d.dtype)
     if residual is not None and residual.stride(-1) != 1:
         residual = residual.contiguous()
-    rc = _lib.try_call("umic_gemm", dev, x2d.data_ptr(), row_stride(x2d), weight.data_ptr(),
-                       row_stride(weight), _lib.ptr(bias), _lib.ptr(residual),
-                       row_stride(residual) if residual is not None else 0, y.data_ptr(), n,
-                       m, n, k, _ACTS[act])
+    ws, ws_bytes = _lib.gemm_workspace(dev, m, n, k) if split_k else (None, 0)
+    args = (x2d.data_ptr(), row_stride(x2d), weight.data_ptr(), row_stride(weight),
+            _lib.ptr(bias), _lib.ptr(residual),
+            row_stride(residual) if residual is not None else 0, y.data_ptr(), n, m, n, k,
+            _ACTS[act])
+    if ws is not None:
+        rc = _lib.try_call("umic_gemm_ws", dev, *args, ws, ws_bytes)
+        stats["umic_gemm_split_k"] += 0 if rc else 1
+    else:
+        rc = _lib.try_call("umic_gemm", dev, *args)
     if rc:
         stats["linear_fallback"] += 1
         return _torch_linear(x2d, weight, bias, act, residual)
