@@ -626,9 +626,13 @@ int check_operand(const char* name, const char* what, const void* p, int64_t ld,
 // Split-K plan of a linear launch: when the output tiles would fill at most half of the
 // CTA pairs (or single CTAs), each tile's k-blocks are cut into `splits` ranges so the work
 // units fill the GPU (at least 4 k-blocks per range, at most 16 ranges). 1 = no split.
+// Counter area at the start of a split-K workspace: one word per tile half for the at
+// most 128 tiles a split launch has (tiles * 2 <= CTA pairs or CTAs).
+constexpr size_t kSplitCounterBytes = 4096;
+
 struct SplitPlan {
   int splits = 1;
-  size_t part_bytes = 0, cnt_offset = 0, bytes = 0;
+  size_t part_bytes = 0, cnt_offset = 0, bytes = 0;  // counters at cnt_offset (0)
 };
 
 SplitPlan plan_split(int64_t m, int64_t n, int64_t k, int units_max) {
@@ -643,9 +647,11 @@ SplitPlan plan_split(int64_t m, int64_t n, int64_t k, int units_max) {
   if (s > 16) s = 16;
   if (s < 2) return sp;
   sp.splits = static_cast<int>(s);
+  // Counters first, at a fixed place whatever the shape (a larger shape's partials must
+  // never land on a later call's counters), then the partials.
+  sp.cnt_offset = 0;
   sp.part_bytes = static_cast<size_t>(tiles) * 2 * s * kBM * kBN * sizeof(float);
-  sp.cnt_offset = (sp.part_bytes + 255) & ~static_cast<size_t>(255);
-  sp.bytes = sp.cnt_offset + ((static_cast<size_t>(tiles) * 2 * 4 + 255) & ~static_cast<size_t>(255));
+  sp.bytes = kSplitCounterBytes + sp.part_bytes;
   return sp;
 }
 
@@ -716,8 +722,8 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
         return fail(UMIC_ERR_INVALID_ARG, "%s: workspace of %zu bytes (256-byte aligned) "
                     "needed, %zu given", name, sp.bytes, workspace_bytes);
       p.splits = sp.splits;
-      p.part = static_cast<float*>(workspace);
-      p.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(workspace) + sp.cnt_offset);
+      p.cnt = static_cast<unsigned*>(workspace);
+      p.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kSplitCounterBytes);
     }
   }
   p.wait_limit = kWaitLimitCycles;
