@@ -87,11 +87,12 @@ struct TcParams {
   long long wait_limit;  // SM cycles a bounded wait may take before the CTA unwinds
   int stall;             // test hook: CTA 0 skips the loads of its first stage
   // Split-K (linear only): each tile's k-blocks are cut into `splits` contiguous ranges,
-  // one work unit each; a unit writes its fp32 partial to `part` and the last of a tile
-  // half's units (counted in `cnt`) sums them in split order and runs the epilogue.
+  // one work unit each; a unit writes its fp32 partial to `part`, waits until the tile
+  // half's other units have written theirs (counted in `cnt`), then sums its share of
+  // the rows in split order and runs the epilogue on them.
   int splits;
   float* part;    // [tiles][2 halves][splits][128 rows][kBN cols]
-  unsigned* cnt;  // [tiles][2 halves], zero between calls
+  unsigned* cnt;  // [tiles][2 halves][arrived, done], zero between calls
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -534,44 +535,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (p.splits > 1) {
-        // count this unit in; the last unit of the tile half sums the partials in split
-        // order (deterministic whatever the arrival order) and runs the epilogue
+        // Every unit of the tile half counts itself in once its partial is written, waits
+        // for the others (all units of a split launch are resident: at most one per SM),
+        // then sums rows [sp * 128 / splits, (sp + 1) * 128 / splits) of the half over the
+        // partials in range order (deterministic) and writes them with the epilogue.
+        unsigned* cnt = p.cnt + static_cast<size_t>(t) * 4 + rank * 2;  // [arrived, done]
         __threadfence();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (quarter == 0 && lane == 0) {
+          asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+          *last_flag = 1;
+          const long long start = clock64();
+          for (uint32_t i = 0;; ++i) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+            if (v >= static_cast<unsigned>(p.splits)) break;
+            if ((i & 63u) == 63u && clock64() - start > p.wait_limit) {
+              *abort_flag = 1;
+              if (p.err) atomicOr(p.err, UMIC_DEVERR_WAIT_TIMEOUT);
+              *last_flag = 0;
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (!*last_flag) break;  // a partner never arrived: unwind
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        const int r_lo = sp * kBM / p.splits, r_hi = (sp + 1) * kBM / p.splits;
+        const int cl = lane * 8;  // this lane's 8 columns of the 256-column half
+        const int gcol = col0 + cl;
+        const float* pbase = part_base + cl;
+        for (int r = r_lo + quarter; r < r_hi; r += 4) {
+          const int grow = mb * G::kTileM + static_cast<int>(rank) * kBM + r;
+          if (grow >= p.m) break;
+          float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+          for (int j = 0; j < p.splits; ++j) {
+            const float4* src = reinterpret_cast<const float4*>(
+                pbase + static_cast<size_t>(j) * kBM * kOutCols + static_cast<size_t>(r) * kOutCols);
+            const float4 a = __ldcg(src), b = __ldcg(src + 1);
+            v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+            v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+          }
+          if (gcol >= p.n) continue;
+          if (p.bias) {
+            float bb[8];
+            unpack8(ld_cached(p.bias + gcol), bb);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] += bb[i];
+          }
+          if (p.epilogue == UMIC_EPI_GELU_ERF) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = gelu_erf(v[i]);
+          } else if (p.epilogue == UMIC_EPI_GELU_TANH) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = gelu_tanh(v[i]);
+          }
+          if (p.residual) {
+            float rr[8];
+            unpack8(ld_stream(p.residual + static_cast<int64_t>(grow) * p.ldr + gcol), rr);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] += rr[i];
+          }
+          st_vec(p.y + static_cast<int64_t>(grow) * p.ldy + gcol, pack8(v));
+        }
+        // the last unit to finish returns both counters to zero (every unit has passed
+        // the wait above by then, so none reads them again)
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (quarter == 0 && lane == 0) {
           unsigned prev;
           asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
                        : "=r"(prev)
-                       : "l"(p.cnt + static_cast<size_t>(t) * 2 + rank)
+                       : "l"(cnt + 1)
                        : "memory");
-          *last_flag = prev == static_cast<unsigned>(p.splits - 1);
-        }
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (*last_flag) {
-          asm volatile("fence.acq_rel.gpu;" ::: "memory");
-#pragma unroll 1
-          for (int c = 0; c < kOutCols; c += 32) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-#pragma unroll 1
-            for (int j = 0; j < p.splits; ++j) {
-              const float4* src = reinterpret_cast<const float4*>(
-                  part_base + static_cast<size_t>(j) * kBM * kOutCols +
-                  static_cast<size_t>(erow) * kOutCols + c);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 q = __ldcg(src + i);
-                v[4 * i] += q.x;
-                v[4 * i + 1] += q.y;
-                v[4 * i + 2] += q.z;
-                v[4 * i + 3] += q.w;
-              }
-            }
-            store_chunk(v, mb, col0 + c);
+          if (prev == static_cast<unsigned>(p.splits - 1)) {
+            cnt[0] = 0;
+            cnt[1] = 0;
           }
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-          if (quarter == 0 && lane == 0) p.cnt[static_cast<size_t>(t) * 2 + rank] = 0;
         }
       }
     }
@@ -626,8 +667,8 @@ int check_operand(const char* name, const char* what, const void* p, int64_t ld,
 // Split-K plan of a linear launch: when the output tiles would fill at most half of the
 // CTA pairs (or single CTAs), each tile's k-blocks are cut into `splits` ranges so the work
 // units fill the GPU (at least 4 k-blocks per range, at most 16 ranges). 1 = no split.
-// Counter area at the start of a split-K workspace: one word per tile half for the at
-// most 128 tiles a split launch has (tiles * 2 <= CTA pairs or CTAs).
+// Counter area at the start of a split-K workspace: two words (arrived, done) per tile
+// half for the at most 128 tiles a split launch has (tiles * 2 <= CTA pairs or CTAs).
 constexpr size_t kSplitCounterBytes = 4096;
 
 struct SplitPlan {
