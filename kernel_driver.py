@@ -15,6 +15,8 @@ Used to capture a single kernel under ncu. Modes and shapes:
   gemv           x [rows=8, 4096], W [12288, 4096]
   vit            the cfg3 encoder after apply(), rows = images (16)
   decode         one graph-replayed cfg4 decode step of rows = 8 episodes
+  flow           one cfg5 flow sample (10 graph-replayed Euler steps of the 18-layer
+                 expert) for rows = 32 episodes over a 3100-token prefix cache
   kv             K/V [8, 8, 3100, 128] appended into [8, 8, 3172, 128]
   attn           flow-step attention: q [rows=32 episodes, 16, 64, 128] over the
                  3164-key prefix of a [32, 8, 3172, 128] cache, lower-right causal mask
@@ -171,6 +173,21 @@ def make(mode: str, rows: int | None):
             with torch.no_grad():
                 vlm(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
         return step
+    if mode == "flow":  # one cfg5 flow sample (10 Euler steps, graph replay) per call
+        from umic_b200 import UmicConfig, apply
+        from umic_b200.extras import _prefix_cache
+        from umic_b200.workloads import (CFG5_EXPERT, PREFILL_TOKENS, AlpamayoStandIn,
+                                         build_text_model, flow_sample)
+
+        e = rows or 32
+        expert = build_text_model(CFG5_EXPERT, device=dev, seed=5)
+        apply(AlpamayoStandIn(torch.nn.Module(), expert=expert),
+              UmicConfig(decode_graph=False, decode_cache=False))
+        x0 = torch.randn(e, 64, CFG5_EXPERT["hidden_size"], device=dev, dtype=bf)
+        cache = _prefix_cache(CFG5_EXPERT["num_hidden_layers"], e,
+                              CFG5_EXPERT["num_key_value_heads"], PREFILL_TOKENS,
+                              CFG5_EXPERT["head_dim"], dev)
+        return lambda: flow_sample(expert, cache, PREFILL_TOKENS, x0, graph=True)
     raise SystemExit(f"unknown mode {mode}")
 
 

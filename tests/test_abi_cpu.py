@@ -137,6 +137,9 @@ def test_gemm_split_plan_on_host():
     expert's projections at 4 episodes get a workspace, the LM prefill shapes none."""
     L = _lib.lib()
     assert L.umic_gemm_workspace_bytes(256, 2048, 2048) > 0
+    # 8 tiles x 2 halves x 8 ranges (the cap: one 32-column chunk per range) x 128 KB
+    # of fp32 partials behind a 4 KB counter area, on a 148-SM B200
+    assert L.umic_gemm_workspace_bytes(256, 2048, 2048) == 4096 + 8 * 2 * 8 * 128 * 1024
     assert L.umic_gemm_workspace_bytes(256, 2048, 8192) > 0
     assert L.umic_gemm_workspace_bytes(24800, 4096, 4096) == 0
     assert L.umic_gemm_workspace_bytes(3100, 4096, 4096) == 0

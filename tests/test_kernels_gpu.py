@@ -453,16 +453,21 @@ def test_gemm(cuda, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k,act,res", [
-    (256, 2048, 2048, None, False),       # the flow expert's q/o at 4 episodes: 8 tiles
+    (256, 2048, 2048, None, False),       # the flow expert's q/o at 4 episodes: 8 tiles, 8 ranges
     (256, 2048, 8192, None, True),        # its down_proj, residual in the epilogue
     (512, 1024, 4096, "gelu_tanh", False),  # bias + GELU after the split sum
     (100, 2048, 2048, None, False),       # single-CTA tiles
-    (300, 520, 1000, None, True),         # ragged rows, columns and k
+    (300, 520, 1000, None, True),         # ragged rows, columns and k: 4 ranges
+    (1024, 2048, 2048, None, False),      # 32 tiles: 2 ranges of 4 chunks each
+    (256, 2048, 768, None, False),        # 3 ranges (chunks 2 / 3 / 3)
+    (256, 2048, 1280, None, True),        # 5 ranges
+    (256, 1024, 1536, None, False),       # 6 ranges
+    (512, 1024, 1792, "gelu", False),     # 7 ranges (6 partner blocks per owned chunk)
 ])
 def test_gemm_split_k(cuda, m, n, k, act, res):
-    """Under-filled tile grids run split-K (fp32 partials summed in range order by the
-    last unit of each tile half): against fp32, against the unsplit kernel, and
-    deterministic from call to call."""
+    """Under-filled tile grids run split-K (each k range of a tile half owns some of its
+    32-column chunks and sums every range's partial of them in range order): against
+    fp32, against the unsplit kernel, and deterministic from call to call."""
     x = _randn(m, k, seed=70, dev=cuda)
     w = _randn(n, k, seed=71, dev=cuda, scale=0.02)
     b = _randn(n, seed=72, dev=cuda) if act else None

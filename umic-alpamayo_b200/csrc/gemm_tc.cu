@@ -53,6 +53,8 @@ constexpr int kBN = 256;   // MMA N (output tile width for linear; 2 x 128 for g
 constexpr int kBK = 64;    // one 128-byte swizzle atom of bf16
 constexpr int kThreads = 192;
 constexpr int kGroupM = 16;
+constexpr int kMaxSplits = 8;  // k ranges per tile at most (split-K): one 32-column
+                               // chunk of the tile at least per range
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 
@@ -87,11 +89,12 @@ struct TcParams {
   long long wait_limit;  // SM cycles a bounded wait may take before the CTA unwinds
   int stall;             // test hook: CTA 0 skips the loads of its first stage
   // Split-K (linear only): each tile's k-blocks are cut into `splits` contiguous ranges,
-  // one work unit each; a unit writes its fp32 partial to `part`, waits until the tile
-  // half's other units have written theirs (counted in `cnt`), then sums its share of
-  // the rows in split order and runs the epilogue on them.
+  // one work unit each; a unit writes its fp32 partial of the column chunks other units
+  // own to `part`, waits until the tile half's other units have written theirs (counted
+  // in `cnt`), then sums its own chunks over all partials in range order and runs the
+  // epilogue on them.
   int splits;
-  float* part;    // [tiles][2 halves][splits][128 rows][kBN cols]
+  float* part;    // [tiles][2 halves][splits][4 warps][8 chunks][8][32 lanes] float4
   unsigned* cnt;  // [tiles][2 halves][arrived, done], zero between calls
 };
 
@@ -182,6 +185,15 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t a, const uint4& v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w) : "memory");
@@ -247,6 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kStages * G::kStageBytes);
   // bars: full[kStages], empty[kStages], acc_full[2], acc_empty[2], drain
+  // bars[2 * kStages + 8 ...+ 11]: split-K partial fetches, one per epilogue warp
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * G::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = abort_flag + 1;  // split-K: this CTA sums the tile half
@@ -257,6 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + G::kStages);
   const uint32_t accf0 = smem_u32(bars + 2 * G::kStages), acce0 = accf0 + 16;
   const uint32_t drain = accf0 + 32;
+  const uint32_t red0 = smem_u32(bars + 2 * G::kStages + 8);
   const uint32_t sbase = smem_u32(smem);
   const int tiles = p.tiles_m * p.tiles_n;
   const int work = tiles * p.splits;  // work units: (tile, k range)
@@ -273,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acce0, 128 * kPair);  // every epilogue thread of the pair
     mbar_init(acce0 + 8, 128 * kPair);
     mbar_init(drain, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(red0 + 8 * q, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -435,6 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t stg0 = sbase + G::kStageOut + quarter * 4096;
     int chunk_idx = 0;
     int it = 0;
+    uint32_t red_phase = 0;  // split-K partial fetch barrier parity
     constexpr int kOutCols = kDual ? kBN / 2 : kBN;
     const int erow = quarter * 32 + lane;  // this thread's accumulator row (TMEM lane)
     // Bias / activation / residual on one 32-column chunk of this thread's row, then the
@@ -503,42 +519,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
       const int col0 = nb * kOutCols;
-      // split-K: this unit's fp32 partial rows [128][kOutCols] of the tile half
-      float* part_base = p.part + (static_cast<size_t>(t) * 2 + rank) * p.splits *
-                                      (static_cast<size_t>(kBM) * kOutCols);
+      if (p.splits == 1) {
 #pragma unroll 1
-      for (int c = 0; c < kOutCols; c += 32) {
-        __syncwarp();  // tcgen05.ld is warp-collective
-        float v[32];
-        tmem_ld32(tbase + c, v);
-        if (kDual) {
-          float u[32];
-          tmem_ld32(tbase + kBN / 2 + c, u);
+        for (int c = 0; c < kOutCols; c += 32) {
+          __syncwarp();  // tcgen05.ld is warp-collective
+          float v[32];
+          tmem_ld32(tbase + c, v);
+          if (kDual) {
+            float u[32];
+            tmem_ld32(tbase + kBN / 2 + c, u);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = silu(v[i]) * u[i];
-        }
-        if (c + 32 >= kOutCols) {
-          // All TMEM reads of this tile are done: hand the buffer back to the MMA.
-          tc_fence_before();
-          if (kPair == 2) mbar_arrive_cluster(lead_acce0 + 8 * acc);
-          else mbar_arrive(acce0 + 8 * acc);
-        }
-        if (p.splits == 1) {
+            for (int i = 0; i < 32; ++i) v[i] = silu(v[i]) * u[i];
+          }
+          if (c + 32 >= kOutCols) {
+            // All TMEM reads of this tile are done: hand the buffer back to the MMA.
+            tc_fence_before();
+            if (kPair == 2) mbar_arrive_cluster(lead_acce0 + 8 * acc);
+            else mbar_arrive(acce0 + 8 * acc);
+          }
           store_chunk(v, mb, col0 + c);
-        } else {
-          float4* dst = reinterpret_cast<float4*>(
-              part_base + static_cast<size_t>(sp) * kBM * kOutCols +
-              static_cast<size_t>(erow) * kOutCols + c);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            __stcg(dst + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
         }
+        continue;
       }
-      if (p.splits > 1) {
-        // Every unit of the tile half counts itself in once its partial is written, waits
-        // for the others (all units of a split launch are resident: at most one per SM),
-        // then sums rows [sp * 128 / splits, (sp + 1) * 128 / splits) of the half over the
-        // partials in range order (deterministic) and writes them with the epilogue.
+      if constexpr (!kDual) {
+        // Split-K (every unit of the launch resident, at most one per CTA). The tile
+        // half's 8 column chunks of 32 are dealt to its `splits` units as contiguous
+        // ranges; a unit stores its partial of every chunk it does not own, counts itself
+        // in, waits for the others, then fetches their partials of its own chunks with
+        // bulk copies into its warp's quarter of the idle stage ring and sums them in unit
+        // order (deterministic) with its own accumulator, still in TMEM.
+        constexpr int kChunks = kOutCols / 32;
+        const int s = p.splits;
+        const int own_lo = sp * kChunks / s, own_hi = (sp + 1) * kChunks / s;
+        // partial block (unit q, warp quarter, chunk): 32 rows x 32 fp32 as [8][32 lanes]
+        // float4, so every warp store / load instruction covers 512 contiguous bytes
+        float4* part_tile = reinterpret_cast<float4*>(p.part) +
+                            (static_cast<size_t>(t) * 2 + rank) * s * 4 * kChunks * 256;
+        auto block = [&](int q, int ci) {
+          return part_tile + ((static_cast<size_t>(q) * 4 + quarter) * kChunks + ci) * 256;
+        };
+#pragma unroll 1
+        for (int ci = 0; ci < kChunks; ++ci) {
+          if (ci >= own_lo && ci < own_hi) continue;
+          __syncwarp();
+          float v[32];
+          tmem_ld32(tbase + ci * 32, v);
+          float4* dst = block(sp, ci) + lane;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            __stcg(dst + j * 32, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+        }
         unsigned* cnt = p.cnt + static_cast<size_t>(t) * 4 + rank * 2;  // [arrived, done]
         __threadfence();
         asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -549,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (uint32_t i = 0;; ++i) {
             unsigned v;
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
-            if (v >= static_cast<unsigned>(p.splits)) break;
+            if (v >= static_cast<unsigned>(s)) break;
             if ((i & 63u) == 63u && clock64() - start > p.wait_limit) {
               *abort_flag = 1;
               if (p.err) atomicOr(p.err, UMIC_DEVERR_WAIT_TIMEOUT);
@@ -561,45 +591,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (!*last_flag) break;  // a partner never arrived: unwind
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        const int r_lo = sp * kBM / p.splits, r_hi = (sp + 1) * kBM / p.splits;
-        const int cl = lane * 8;  // this lane's 8 columns of the 256-column half
-        const int gcol = col0 + cl;
-        const float* pbase = part_base + cl;
-        for (int r = r_lo + quarter; r < r_hi; r += 4) {
-          const int grow = mb * G::kTileM + static_cast<int>(rank) * kBM + r;
-          if (grow >= p.m) break;
-          float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-          for (int j = 0; j < p.splits; ++j) {
-            const float4* src = reinterpret_cast<const float4*>(
-                pbase + static_cast<size_t>(j) * kBM * kOutCols + static_cast<size_t>(r) * kOutCols);
-            const float4 a = __ldcg(src), b = __ldcg(src + 1);
-            v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
-            v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
-          }
-          if (gcol >= p.n) continue;
-          if (p.bias) {
-            float bb[8];
-            unpack8(ld_cached(p.bias + gcol), bb);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] += bb[i];
-          }
-          if (p.epilogue == UMIC_EPI_GELU_ERF) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = gelu_erf(v[i]);
-          } else if (p.epilogue == UMIC_EPI_GELU_TANH) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = gelu_tanh(v[i]);
-          }
-          if (p.residual) {
-            float rr[8];
-            unpack8(ld_stream(p.residual + static_cast<int64_t>(grow) * p.ldr + gcol), rr);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] += rr[i];
-          }
-          st_vec(p.y + static_cast<int64_t>(grow) * p.ldy + gcol, pack8(v));
+        const uint32_t region = sbase + quarter * (G::kStages * G::kStageBytes / 4);
+        const uint32_t rbar = red0 + 8 * quarter;
+        if (lane == 0) {
+          // the partials were written through the generic proxy by other SMs; order
+          // their (acquired) visibility before this thread's async-proxy reads
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          mbar_expect_tx(rbar, static_cast<uint32_t>((own_hi - own_lo) * (s - 1)) * 4096u);
+          uint32_t slot = 0;
+          for (int ci = own_lo; ci < own_hi; ++ci)
+            for (int q = 0; q < s; ++q)
+              if (q != sp) bulk_load(region + 4096u * slot++, block(q, ci), 4096u, rbar);
         }
+        if (!mbar_wait(rbar, red_phase, p.err, abort_flag, p.wait_limit)) {
+          // copies may still be in flight into this shared memory: let them land
+          const long long t0 = clock64();
+          while (clock64() - t0 < 4000000LL) {
+          }
+          break;
+        }
+        red_phase ^= 1;
+        uint32_t slot = 0;
+#pragma unroll 1
+        for (int ci = own_lo; ci < own_hi; ++ci) {
+          __syncwarp();
+          float mine[32];
+          tmem_ld32(tbase + ci * 32, mine);
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+#pragma unroll 1
+          for (int q = 0; q < s; ++q) {
+            if (q == sp) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += mine[i];
+            } else {
+              const uint32_t src = region + 4096u * slot++ + lane * 16;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 f = lds_f4(src + j * 512);
+                v[4 * j] += f.x;
+                v[4 * j + 1] += f.y;
+                v[4 * j + 2] += f.z;
+                v[4 * j + 3] += f.w;
+              }
+            }
+          }
+          store_chunk(v, mb, col0 + ci * 32);
+        }
+        tc_fence_before();
+        if (kPair == 2) mbar_arrive_cluster(lead_acce0 + 8 * acc);
+        else mbar_arrive(acce0 + 8 * acc);
         // the last unit to finish returns both counters to zero (every unit has passed
         // the wait above by then, so none reads them again)
         asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -609,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        : "=r"(prev)
                        : "l"(cnt + 1)
                        : "memory");
-          if (prev == static_cast<unsigned>(p.splits - 1)) {
+          if (prev == static_cast<unsigned>(s - 1)) {
             cnt[0] = 0;
             cnt[1] = 0;
           }
@@ -666,7 +709,7 @@ int check_operand(const char* name, const char* what, const void* p, int64_t ld,
 
 // Split-K plan of a linear launch: when the output tiles would fill at most half of the
 // CTA pairs (or single CTAs), each tile's k-blocks are cut into `splits` ranges so the work
-// units fill the GPU (at least 4 k-blocks per range, at most 16 ranges). 1 = no split.
+// units fill the GPU (at least 4 k-blocks per range, at most 8 ranges). 1 = no split.
 // Counter area at the start of a split-K workspace: two words (arrived, done) per tile
 // half for the at most 128 tiles a split launch has (tiles * 2 <= CTA pairs or CTAs).
 constexpr size_t kSplitCounterBytes = 4096;
@@ -685,7 +728,7 @@ SplitPlan plan_split(int64_t m, int64_t n, int64_t k, int units_max) {
   if (tiles <= 0 || tiles * 2 > units_max || kblocks < 8) return sp;
   int64_t s = units_max / tiles;
   if (s > kblocks / 4) s = kblocks / 4;
-  if (s > 16) s = 16;
+  if (s > kMaxSplits) s = kMaxSplits;
   if (s < 2) return sp;
   sp.splits = static_cast<int>(s);
   // Counters first, at a fixed place whatever the shape (a larger shape's partials must
