@@ -274,6 +274,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // set-up above overlaps the previous kernel's tail (launch_pdl); its outputs (q, the
+  // KV cache, the mask bits) are read only after it has completed
+  allow_dependent_launch();
+  wait_prerequisite();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -588,6 +592,8 @@ __global__ void __launch_bounds__(256) mask_pack_kernel(const uint8_t* __restric
                                                         uint32_t* __restrict__ bits,
                                                         int64_t wb, int64_t wh, int64_t wt,
                                                         int64_t rows) {
+  allow_dependent_launch();
+  wait_prerequisite();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -712,9 +718,10 @@ extern "C" int umic_attention_rows(const void* q, int64_t q_sb, int64_t q_sh, in
   });
   if (e != cudaSuccess)
     return fail(UMIC_ERR_LAUNCH, "%s: smem attribute: %s", kName, cudaGetErrorString(e));
-  attn_rows_kernel<<<static_cast<unsigned>(batch * hkv * qtiles), kThreads, kSmem,
-                     as_stream(stream)>>>(
-      mq, mk, mv, p);
+  const dim3 grid(static_cast<unsigned>(batch * hkv * qtiles));
+  const cudaError_t le =
+      launch_pdl(attn_rows_kernel, grid, dim3(kThreads), kSmem, as_stream(stream), mq, mk, mv, p);
+  if (le != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", kName, cudaGetErrorString(le));
   return launch_status(kName);
 }
 
@@ -734,8 +741,10 @@ extern "C" int umic_mask_pack_bits(const void* mask, int64_t sb, int64_t sh, int
       rows > (int64_t{1} << 40))
     return fail(UMIC_ERR_UNSUPPORTED, "%s: size too large", kName);
   const int64_t blocks = (rows + 7) / 8;
-  mask_pack_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+  const cudaError_t le = launch_pdl(
+      mask_pack_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, as_stream(stream),
       static_cast<const uint8_t*>(mask), sb, sh, st, static_cast<int>(heads), static_cast<int>(t),
       static_cast<int>(lk), bits, wb, wh, wt, rows);
+  if (le != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", kName, cudaGetErrorString(le));
   return launch_status(kName);
 }

@@ -55,6 +55,27 @@ inline void prefer_max_shared() {
 }
 
 // Maps the launch status to UMIC_ERR_LAUNCH with the CUDA error string.
+// Launches `kernel` with programmatic stream serialization: its CTAs may become
+// resident while the previous kernel of the stream finishes (once that kernel has
+// called griddepcontrol.launch_dependents), so the launch latency hides behind its
+// tail. The kernel must call wait_prerequisite() before it reads anything the previous
+// kernel writes (or writes anything that kernel reads).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 inline int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
@@ -69,6 +90,12 @@ inline int launch_status(const char* what) {
 // this grid writes; without such a dependent this is a no-op.
 __device__ __forceinline__ void allow_dependent_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Waits until the previous kernel of the stream has completed and its writes are
+// visible (a no-op unless this grid was launched with launch_pdl).
+__device__ __forceinline__ void wait_prerequisite() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // Eight bf16 values travel as one 16-byte vector.

@@ -313,6 +313,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The set-up above overlaps the previous kernel's tail (the launch allows it); the
+  // operands, the output and the split-K workspace are touched only after it completed.
+  allow_dependent_launch();
+  wait_prerequisite();
   // The leader's barriers as seen from either CTA of the pair.
   const uint32_t lead_full0 = kPair == 2 ? cluster_addr(full0, 0) : full0;
   const uint32_t lead_acce0 = kPair == 2 ? cluster_addr(acce0, 0) : acce0;
@@ -826,7 +830,9 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   if (!pair) {
     if (int rc = set_smem_attr<kDual, 1>()) return rc;
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-    tc_gemm_kernel<kDual, 1><<<grid, kThreads, Geo<1>::kSmem, st>>>(ma, mb, mb2, my, p);
+    const cudaError_t le = launch_pdl(tc_gemm_kernel<kDual, 1>, dim3(grid), dim3(kThreads),
+                                      Geo<1>::kSmem, st, ma, mb, mb2, my, p);
+    if (le != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", name, cudaGetErrorString(le));
     return launch_status(name);
   }
   if (int rc = set_smem_attr<kDual, 2>()) return rc;
@@ -836,13 +842,16 @@ int run(const char* name, const void* x, int64_t ldx, const void* w, int64_t ldw
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = Geo<2>::kSmem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // programmatic stream serialization: see the grid dependency wait in the kernel
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<kDual, 2>, ma, mb, mb2, my, p);
   if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", name, cudaGetErrorString(e));
   return launch_status(name);

@@ -46,6 +46,7 @@ __device__ __forceinline__ bool resolve_pos(const KvArgs& a, int64_t& pos) {
 template <bool kVec>
 __global__ void __launch_bounds__(256) kv_append_kernel(KvArgs a) {
   allow_dependent_launch();
+  wait_prerequisite();
   int64_t pos;
   if (!resolve_pos(a, pos)) return;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.y + threadIdx.y;
@@ -107,7 +108,7 @@ extern "C" int umic_kv_append(void* k_buf, void* v_buf, int64_t buf_sb, int64_t 
                   static_cast<unsigned>(batch));
   const dim3 block(bx, by);
   cudaStream_t st = as_stream(stream);
-  if (vec) kv_append_kernel<true><<<grid, block, 0, st>>>(a);
-  else kv_append_kernel<false><<<grid, block, 0, st>>>(a);
+  if (vec) launch_pdl(kv_append_kernel<true>, grid, block, 0, st, a);
+  else launch_pdl(kv_append_kernel<false>, grid, block, 0, st, a);
   return launch_status("umic_kv_append");
 }

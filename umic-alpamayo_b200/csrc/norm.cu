@@ -64,6 +64,7 @@ __device__ __forceinline__ float group_sum(float v, float* red) {
 template <int TPR, int VPT, bool kAdd, bool kLayerNorm, bool kAxpy = false>
 __global__ void __launch_bounds__(kThreads) norm_vec_kernel(NormArgs a) {
   allow_dependent_launch();
+  wait_prerequisite();
   constexpr int kRowsPerCta = kThreads / TPR;
   __shared__ float red[kThreads / 32];
   const int sub = threadIdx.x % TPR;
@@ -194,8 +195,8 @@ void launch_vec(const NormArgs& a, cudaStream_t st) {
   constexpr int kRowsPerCta = kThreads / TPR;
   const int64_t grid = (a.rows + kRowsPerCta - 1) / kRowsPerCta;
   prefer_max_shared<norm_vec_kernel<TPR, VPT, kAdd, kLN, kAxpy>>();
-  norm_vec_kernel<TPR, VPT, kAdd, kLN, kAxpy>
-      <<<static_cast<unsigned>(grid), kThreads, 0, st>>>(a);
+  launch_pdl(norm_vec_kernel<TPR, VPT, kAdd, kLN, kAxpy>, dim3(static_cast<unsigned>(grid)),
+             dim3(kThreads), 0, st, a);
 }
 
 template <bool kAdd, bool kLN, bool kAxpy = false>

@@ -65,6 +65,7 @@ constexpr int kPrepThreads = 128;
 template <int TPH, bool kCosFp32>
 __global__ void __launch_bounds__(kPrepThreads) qk_prep_kernel(PrepArgs a) {
   allow_dependent_launch();
+  wait_prerequisite();
   constexpr int kRowsPerBlock = kPrepThreads / TPH;
   constexpr int kHalfD = TPH * 8;  // D / 2
   const int sub = threadIdx.x % TPH;
@@ -155,10 +156,10 @@ void launch_prep(const PrepArgs& a, int64_t seq, int64_t batch, int zblocks, boo
                   static_cast<unsigned>(zblocks));
   if (cos32) {
     prefer_max_shared<qk_prep_kernel<TPH, true>>();
-    qk_prep_kernel<TPH, true><<<grid, kPrepThreads, 0, st>>>(a);
+    launch_pdl(qk_prep_kernel<TPH, true>, grid, dim3(kPrepThreads), 0, st, a);
   } else {
     prefer_max_shared<qk_prep_kernel<TPH, false>>();
-    qk_prep_kernel<TPH, false><<<grid, kPrepThreads, 0, st>>>(a);
+    launch_pdl(qk_prep_kernel<TPH, false>, grid, dim3(kPrepThreads), 0, st, a);
   }
 }
 

@@ -61,6 +61,7 @@ __device__ __forceinline__ __nv_bfloat16* locate(const RopeArgs& a, int64_t& cro
 template <bool kCosFp32>
 __global__ void __launch_bounds__(1024) rope_vec_kernel(RopeArgs a) {
   allow_dependent_launch();
+  wait_prerequisite();
   int64_t crow;
   __nv_bfloat16* row = locate(a, crow);
   if (!row) return;
@@ -85,6 +86,7 @@ __global__ void __launch_bounds__(1024) rope_vec_kernel(RopeArgs a) {
 // Any even head_dim / alignment: one rotation pair per thread.
 __global__ void __launch_bounds__(1024) rope_scalar_kernel(RopeArgs a, bool cos_fp32) {
   allow_dependent_launch();
+  wait_prerequisite();
   int64_t crow;
   __nv_bfloat16* row = locate(a, crow);
   if (!row) return;
@@ -145,10 +147,10 @@ extern "C" int umic_rope_inplace(void* q, int64_t q_sb, int64_t q_ss, int64_t q_
                   static_cast<unsigned>((heads + by - 1) / by));
   cudaStream_t st = as_stream(stream);
   if (vec) {
-    if (fp32) rope_vec_kernel<true><<<grid, block, 0, st>>>(a);
-    else rope_vec_kernel<false><<<grid, block, 0, st>>>(a);
+    if (fp32) launch_pdl(rope_vec_kernel<true>, grid, block, 0, st, a);
+    else launch_pdl(rope_vec_kernel<false>, grid, block, 0, st, a);
   } else {
-    rope_scalar_kernel<<<grid, block, 0, st>>>(a, fp32);
+    launch_pdl(rope_scalar_kernel, grid, block, 0, st, a, fp32);
   }
   return launch_status("umic_rope_inplace");
 }
