@@ -181,11 +181,11 @@ def test_lm_decode_token_stream(cuda):
     assert e_ours <= max(1e-2, 1.05 * e_eager)
 
 
-@pytest.mark.parametrize("images", [2])
+@pytest.mark.parametrize("images", [2, 16])
 def test_vit_forward_vs_fp32(cuda, images):
     """cfg3 ViT (27 blocks, hidden 1280, 16 x 80 heads, tanh-GELU 5120) on 448 x 448
     images through the fused pipeline (patch-embed GEMM, add+LayerNorm, in-place
-    vision RoPE, packed varlen attention)."""
+    vision RoPE, packed varlen attention); 16 images is the cfg3 batch (16 384 patches)."""
     vis = build_vision_model(device=cuda)
     pix, grid = vit_inputs(images=images, device=cuda)
     ref32 = copy.deepcopy(vis).float()
@@ -229,14 +229,16 @@ def _prefix_cache(layers, episodes, heads, tokens, dim, dev, dtype, seed=30):
     return c
 
 
-def test_flow_expert_euler(cuda):
+@pytest.mark.parametrize("E", [4, 32])
+def test_flow_expert_euler(cuda, E):
     """cfg5: the 18-layer expert (hidden 2048, GQA 16/8 x 128, SwiGLU 8192) runs 10 Euler
     steps of 64 action tokens per episode over a 3100-token prefix KV that is
     appended to and cropped back every step. The patched expert (fused MLP / q-o
-    GEMMs, norms, in-place RoPE, in-place KV through the repeat-cache hook) vs fp32."""
+    GEMMs, norms, in-place RoPE, in-place KV through the repeat-cache hook) vs fp32.
+    32 episodes is the cfg5 batch; 4 is one rank's share at 8 GPUs (split-K GEMMs)."""
     from umic_b200.workloads import CFG5_EXPERT, build_text_model, flow_sample
 
-    E, T, S = 4, 64, 3100
+    T, S = 64, 3100
     expert = build_text_model(CFG5_EXPERT, device=cuda, seed=5)
     g = torch.Generator().manual_seed(31)
     x0 = torch.randn(E, T, 2048, generator=g).to(cuda)
