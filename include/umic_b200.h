@@ -335,7 +335,8 @@ UMIC_API int umic_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, c
  * sums the partials in range order (deterministic) and runs the epilogue (bias, GELU,
  * residual). Other shapes run exactly as umic_gemm. workspace: at least
  * umic_gemm_workspace_bytes(m, n, k) bytes (0 when no split applies), 256-byte aligned,
- * zero-filled before its first use; every call leaves its counters at zero. Calls sharing
+ * zero-filled before its first use; every call leaves its counters at zero, except a call
+ * that set UMIC_DEVERR_WAIT_TIMEOUT: zero the workspace again after one. Calls sharing
  * a workspace must be ordered on one stream. Replaces linear_triton (linear.py:118-145)
  * for the small-row shapes the reference sent to cuBLAS. */
 UMIC_API int umic_gemm_ws(const void* x, int64_t ldx, const void* w, int64_t ldw,

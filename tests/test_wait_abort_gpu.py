@@ -35,13 +35,23 @@ def _stalled(cuda, kernel, fn):
 
 
 @pytest.mark.parametrize("m", [512, 100])  # CTA pairs, and single CTAs (m <= 128)
-def test_gemm_wait_timeout_unwinds(cuda, m):
+@pytest.mark.parametrize("split_k", [True, False])
+def test_gemm_wait_timeout_unwinds(cuda, m, split_k):
+    """Both shapes run split-K when allowed (6 / 3 output tiles): the stalled unit never
+    counts in, its partners give up on the count, and the workspace keeps their stale
+    counts until it is zeroed; the next calls -- with new inputs, so no leftover partial
+    can pass for a fresh one -- are correct."""
     x = _randn(m, 1024, seed=1, dev=cuda)
     w = _randn(768, 1024, seed=2, dev=cuda, scale=0.05)
-    ref = linear(x, w).clone()
-    _stalled(cuda, 1, lambda: linear(x, w))
-    for _ in range(3):
-        assert torch.equal(linear(x, w), ref)
+    assert (_lib.lib().umic_gemm_workspace_bytes(m, 768, 1024) > 0)
+    _stalled(cuda, 1, lambda: linear(x, w, split_k=split_k))
+    _lib.zero_gemv_workspaces()  # counters of a split launch that unwound
+    for seed in (10, 11, 12):
+        x2 = _randn(m, 1024, seed=seed, dev=cuda)
+        ref = torch.nn.functional.linear(x2.float(), w.float())
+        y = linear(x2, w, split_k=split_k)
+        assert (y.float() - ref).norm() / ref.norm() < 1e-2
+        assert torch.equal(y, linear(x2, w, split_k=split_k))
     assert _lib.device_errors(cuda, clear=True) == 0
 
 
