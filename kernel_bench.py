@@ -1,6 +1,8 @@
 """Single-kernel micro-benchmark of the library against cuBLAS / eager torch.
 
     python kernel_bench.py [--out results.json]
+    python kernel_bench.py --reference [--out results.json]   (the reference's own Triton
+        kernels, from its offline install in baseline/_ref, beside this build's)
 
 Each case is timed with CUDA events around one launch after 3 warm-up launches,
 with a 256 MB buffer read between launches to flush L2 (a read leaves no dirty
@@ -148,5 +150,115 @@ def main() -> None:
         json.dump(res, open(sys.argv[sys.argv.index("--out") + 1], "w"), indent=1)
 
 
+def reference_side_by_side() -> dict:
+    """The reference's own Triton kernels (its `umic` package, installed offline into
+    baseline/_ref) beside this build's kernels, on the BASELINE cfg1 / cfg2 shapes and the
+    q/o projection, timed the same way (one launch between L2 flushes, median of 20).
+    Also reports the relative L2 difference between the two outputs."""
+    ref_dir = _ROOT / "baseline" / "_ref"
+    if not (ref_dir / "umic").is_dir():
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    sys.path.insert(0, str(ref_dir))
+    from umic.kernels import fused_ffn as rf_ffn, layernorm as rf_ln, linear as rf_lin, \
+        rmsnorm as rf_rms, rope as rf_rope
+
+    if not rf_ffn.HAS_TRITON:
+        return {"unavailable": "Triton did not import in the reference package"}
+    dev = torch.device("cuda", 0)
+    bf = torch.bfloat16
+    flush = torch.ones(64 * 1024 * 1024, dtype=torch.int32, device=dev)
+
+    def t(fn, iters=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            flush.sum()
+            s0 = torch.cuda.Event(enable_timing=True)
+            e0 = torch.cuda.Event(enable_timing=True)
+            s0.record()
+            fn()
+            e0.record()
+            torch.cuda.synchronize()
+            ts.append(s0.elapsed_time(e0))
+        ts.sort()
+        return ts[len(ts) // 2]
+
+    def rel(a, b):
+        return float((a.float() - b.float()).norm() / b.float().norm())
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    res = {}
+
+    def row(name, ours, theirs, units, work, pick=lambda o: o):
+        ms_o, ms_t = t(ours), t(theirs)
+        res[name] = {"ours_ms": ms_o, "reference_triton_ms": ms_t, "speedup": ms_t / ms_o,
+                     units: [work / (ms_o * 1e-3), work / (ms_t * 1e-3)],
+                     "rel_l2_diff": rel(pick(ours()), pick(theirs()))}
+
+    # cfg1 gate/up (fused SiLU-mul) and the q/o projection at one episode
+    x = torch.randn(3100, 4096, device=dev, dtype=bf, generator=g)
+    wg = torch.randn(12288, 4096, device=dev, dtype=bf, generator=g) * 0.02
+    wu = torch.randn(12288, 4096, device=dev, dtype=bf, generator=g) * 0.02
+    row("gate_silu_mul_3100x12288x4096", lambda: gate_silu_mul_nk(x, wg, wu),
+        lambda: rf_ffn.gate_silu_mul(x, wg.t(), wu.t()), "tflops", 4.0 * 3100 * 12288 * 4096 / 1e12)
+    wq = torch.randn(4096, 4096, device=dev, dtype=bf, generator=g) * 0.02
+    row("linear_3100x4096x4096", lambda: linear(x, wq), lambda: rf_lin.linear_triton(x, wq),
+        "tflops", 2.0 * 3100 * 4096 * 4096 / 1e12)
+    wd = torch.randn(4096, 12288, device=dev, dtype=bf, generator=g) * 0.02
+    h = torch.randn(3100, 12288, device=dev, dtype=bf, generator=g)
+    row("linear_3100x4096x12288", lambda: linear(h, wd), lambda: rf_lin.linear_triton(h, wd),
+        "tflops", 2.0 * 3100 * 4096 * 12288 / 1e12)
+    # cfg2 (a) add+RMSNorm, (b) add+LayerNorm, (c) text RoPE, (d) vision RoPE
+    r = torch.randn_like(x)
+    w = (1 + 0.05 * torch.randn(4096, device=dev, generator=g)).to(bf)
+    row("add_rmsnorm_3100x4096", lambda: add_rmsnorm(x, r, w, 1e-6),
+        lambda: rf_rms.add_rmsnorm_triton(x, r, w, 1e-6), "gbs", 101.6e6 / 1e9,
+        pick=lambda o: o[0])
+    xv = torch.randn(16384, 1280, device=dev, dtype=bf, generator=g)
+    rv = torch.randn_like(xv)
+    wv = torch.ones(1280, device=dev, dtype=bf)
+    bv = torch.zeros(1280, device=dev, dtype=bf)
+    row("add_layernorm_16384x1280", lambda: add_layernorm(xv, rv, wv, bv, 1e-6),
+        lambda: rf_ln.add_layernorm_triton(xv, rv, wv, bv, 1e-6), "gbs", 167.8e6 / 1e9,
+        pick=lambda o: o[0])
+    q = torch.randn(1, 3100, 32, 128, device=dev, dtype=bf, generator=g).transpose(1, 2)
+    k = torch.randn(1, 3100, 8, 128, device=dev, dtype=bf, generator=g).transpose(1, 2)
+    cos = torch.randn(1, 3100, 128, device=dev, dtype=bf, generator=g)
+    sin = torch.randn_like(cos)
+    text_rope = rf_rope.make_text_rope(None)
+    q2, k2 = q.clone(), k.clone()
+    ms_o = t(lambda: apply_rotary_text_inplace(q2, k2, cos, sin))
+    ms_t = t(lambda: text_rope(q, k, cos, sin))
+    q3, k3 = q.clone(), k.clone()
+    apply_rotary_text_inplace(q3, k3, cos, sin)
+    qr, kr = text_rope(q, k, cos, sin)
+    res["text_rope_3100"] = {"ours_ms": ms_o, "reference_triton_ms": ms_t, "speedup": ms_t / ms_o,
+                             "gbs": [65.1e6 / (ms_o * 1e-3) / 1e9, 65.1e6 / (ms_t * 1e-3) / 1e9],
+                             "rel_l2_diff": max(rel(q3, qr), rel(k3, kr))}
+    qkv = torch.randn(16384, 3, 16, 80, device=dev, dtype=bf, generator=g)
+    qq, kk, _ = qkv.unbind(1)
+    cv = torch.randn(16384, 80, device=dev, generator=g)
+    sv = torch.randn_like(cv)
+    ms_o = t(lambda: apply_rotary_vision(qq, kk, cv, sv))
+    ms_t = t(lambda: rf_rope.apply_rotary_vision_triton(qq, kk, cv, sv))
+    q4, k4 = qq.clone(), kk.clone()
+    apply_rotary_vision(q4, k4, cv, sv)
+    qr, kr = rf_rope.apply_rotary_vision_triton(qq, kk, cv, sv)
+    res["vision_rope_16384"] = {"ours_ms": ms_o, "reference_triton_ms": ms_t,
+                                "speedup": ms_t / ms_o,
+                                "gbs": [2 * 94.4e6 / (ms_o * 1e-3) / 1e9,
+                                        2 * 94.4e6 / (ms_t * 1e-3) / 1e9],
+                                "rel_l2_diff": max(rel(q4, qr), rel(k4, kr))}
+    return res
+
+
 if __name__ == "__main__":
-    main()
+    if "--reference" in sys.argv:
+        out = reference_side_by_side()
+        print(json.dumps(out, indent=1))
+        if "--out" in sys.argv:
+            json.dump(out, open(sys.argv[sys.argv.index("--out") + 1], "w"), indent=1)
+    else:
+        main()
