@@ -54,7 +54,6 @@ inline void prefer_max_shared() {
   });
 }
 
-// Maps the launch status to UMIC_ERR_LAUNCH with the CUDA error string.
 // Launches `kernel` with programmatic stream serialization: its CTAs may become
 // resident while the previous kernel of the stream finishes (once that kernel has
 // called griddepcontrol.launch_dependents), so the launch latency hides behind its
@@ -76,6 +75,8 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// Maps the launch status to UMIC_ERR_LAUNCH with the CUDA error string (a failed
+// cudaLaunchKernelEx is reported here too: it sets the runtime's last error).
 inline int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(UMIC_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
