@@ -28,12 +28,14 @@ from __future__ import annotations
 
 import argparse
 import datetime
+import faulthandler
 import json
 import os
 import statistics
 import subprocess
 import sys
 import threading
+import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -176,16 +178,47 @@ def run_reference(args) -> None:
 
 # -------------------------------------------------------------------- GPU arm
 
+class Progress:
+    """Multi-rank runs only: a line on stderr as each rank begins a phase, and a
+    watchdog that dumps every thread's Python stack to stderr when no new phase has
+    begun for `stall_s` seconds, so that a rank which stops shows where."""
+
+    def __init__(self, rank: int, world: int, stall_s: float = 240.0):
+        self.on = world > 1
+        self.rank = rank
+        self.stall_s = stall_s
+        self.t0 = time.monotonic()
+
+    def __call__(self, phase: str) -> None:
+        if not self.on:
+            return
+        print(f"[bench rank {self.rank} +{time.monotonic() - self.t0:.1f}s] {phase}",
+              file=sys.stderr, flush=True)
+        faulthandler.dump_traceback_later(self.stall_s, repeat=True, file=sys.__stderr__)
+
+    def close(self) -> None:
+        if self.on:
+            faulthandler.cancel_dump_traceback_later()
+
+
 class Ranks:
     """Host-side coordination of the ranks: barriers and max-over-ranks through a gloo
     group (CPU tensors). Nothing on the data path is exchanged."""
+
+    # A rank that waits this long for the others ends with an error instead of waiting on.
+    TIMEOUT_S = 300
 
     def __init__(self, world: int):
         self.world = world
         if world > 1:
             import torch.distributed as dist
 
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+            # All ranks share one host. Without an interface named, gloo binds to the
+            # address the host name resolves to, which on an isolated box need not be
+            # reachable even from the same host; the loopback device always is.
+            if os.environ.get("MASTER_ADDR", "127.0.0.1") in ("127.0.0.1", "localhost"):
+                os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=self.TIMEOUT_S))
             self.dist = dist
 
     def barrier(self) -> None:
@@ -256,7 +289,10 @@ def run_umic(args) -> None:
     world, rank, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    progress = Progress(rank, world)
+    progress("joining the group")
     ranks = Ranks(world)
+    progress("building the model")
 
     from umic_b200 import UmicConfig, apply
     from umic_b200.kernels import _common as kc
@@ -283,12 +319,14 @@ def run_umic(args) -> None:
                 out = vlm(input_ids=ids, use_cache=True, logits_to_keep=1)
             return out.logits[:, -1].argmax(-1)
 
+        progress("unfused eager steps")
         ref_next = eager_step().clone()
         eager_step()
         n_e = max(2, args.steps // 2)
         ms = _timed(ranks, eager_step, n_e) / n_e
         eager = {"value": TOTAL_EPISODES * TOKENS / (ms / 1e3), "ms_per_step": ms,
                  "what": "unpatched HF modules + DynamicCache, bf16, SDPA, same weights/inputs"}
+    progress("apply and warm-up")
     model = AlpamayoStandIn(vlm)
     report = apply(model, UmicConfig(max_new_tokens=n_decode + 8))
 
@@ -301,6 +339,7 @@ def run_umic(args) -> None:
         parity["first_token_match"] = f"{int((nxt == ref_next).sum())}/{episodes}"
     before = sum(v for k, v in kc.stats.items() if k.startswith("umic_"))
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    progress("timed prefill steps")
     clocks = ClockSampler(vis.split(",")[local] if vis else local)
     clocks.start()
     kc.start_probe("umic_gemm_gate_silu_mul")
@@ -321,6 +360,7 @@ def run_umic(args) -> None:
         n = step()
         nxt_host.copy_(n, non_blocking=True)
 
+    progress("end-to-end steps")
     e2e_ms = _timed(ranks, e2e_step, args.steps) / args.steps
     e2e_value = TOTAL_EPISODES * TOKENS / (e2e_ms / 1e3)
 
@@ -346,8 +386,10 @@ def run_umic(args) -> None:
 
         # pass 1: eager warm-up steps + capture of the other lengths; pass 2 captures the
         # warm-up lengths; pass 3 replays every step
+        progress("decode: capture passes")
         decode_run()
         decode_run()
+        progress("decode: replay pass")
         ranks.barrier()
         dms = ranks.max(decode_run())
         decode = {"steps": n_decode, "ms_per_step": dms / n_decode,
@@ -372,7 +414,9 @@ def run_umic(args) -> None:
     # ---- cfg5 flow, sharded over the ranks
     del cache
     torch.cuda.empty_cache()
+    progress("flow")
     flow = _flow_dp(ranks, dev, rank, world) if not args.skip_flow else {}
+    progress("report")
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -399,6 +443,7 @@ def run_umic(args) -> None:
             line["flow"] = {**extras.pop("flow", {}), **flow}
             line.update(extras)
         print(json.dumps(line), flush=True)
+    progress.close()
     ranks.close()
 
 

@@ -61,6 +61,23 @@ def bench_ranks(rank, world, port, out):
         flow = bench._share(bench.FLOW_EPISODES, rank, world)
         ranks.barrier()
         m = ranks.max(float(flow[1] * 10 + rank))
-        out.put((rank, lm, flow, m))
+        out.put((rank, lm, flow, m, os.environ.get("GLOO_SOCKET_IFNAME")))
     finally:
         ranks.close()
+
+
+def progress_stall(path):
+    """bench.py's Progress on a rank of a 2-rank job whose phase outlasts the watchdog:
+    stderr (fd 2) goes to `path`."""
+    import time
+
+    fd = os.open(path, os.O_WRONLY | os.O_CREAT | os.O_TRUNC, 0o644)
+    os.dup2(fd, 2)
+    import bench
+
+    progress = bench.Progress(rank=1, world=2, stall_s=0.5)
+    progress("a phase that stalls")
+    time.sleep(1.3)
+    progress("the next phase")
+    progress.close()
+    time.sleep(0.8)  # cancelled: no further dump

@@ -74,10 +74,11 @@ def test_gloo_world_size_2_barrier_and_max():
     assert out[0][2] == [[0, 1, 2, 3], [4, 5, 6, 7]]
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 8])
 def test_bench_gloo_ranks_shard_cfg4_and_cfg5(world):
     """bench.py's Ranks on a gloo group: every cfg4 (8) and cfg5 (32) episode lands on
-    exactly one rank in contiguous blocks, and the max over ranks reaches every rank."""
+    exactly one rank in contiguous blocks, and the max over ranks reaches every rank.
+    With a loopback master address the group runs over the loopback device."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -98,3 +99,21 @@ def test_bench_gloo_ranks_shard_cfg4_and_cfg5(world):
     flow_counts = [row[2][1] for row in out]
     expect = max(c * 10 + r for r, c in enumerate(flow_counts))
     assert all(row[3] == expect for row in out)
+    assert all(row[4] == "lo" for row in out)
+
+
+def test_bench_progress_watchdog(tmp_path):
+    """bench.py's phase markers and stall watchdog: a phase that outlasts the watchdog's
+    limit gets the rank's Python stack on stderr; after close() nothing more is dumped."""
+    path = tmp_path / "stderr.txt"
+    p = mp.get_context("spawn").Process(target=dp_workers.progress_stall, args=(str(path),))
+    p.start()
+    p.join(timeout=120)
+    assert p.exitcode == 0
+    text = path.read_text()
+    assert "[bench rank 1 +" in text and "] a phase that stalls" in text
+    assert "] the next phase" in text
+    dumps = text.count("progress_stall")
+    assert 1 <= dumps <= 3  # one or two dumps during the 1.3 s stall, none after close()
+    assert text.index("a phase that stalls") < text.index("progress_stall") < text.index(
+        "the next phase")
