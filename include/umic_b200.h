@@ -330,10 +330,16 @@ UMIC_API int umic_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, c
 /* umic_gemm with a caller workspace that enables split-K for shapes whose output tiles
  * would leave most of the GPU idle (at most half the CTA pairs busy: e.g. the flow
  * expert's q/o/down projections over 4 episodes, 256 rows x 2048 columns = 8 tiles for
- * 74 CTA pairs). Each tile's k-blocks are then cut into up to 16 ranges, one work unit
- * each; a unit writes its fp32 partial to the workspace and the last unit of a tile half
- * sums the partials in range order (deterministic) and runs the epilogue (bias, GELU,
- * residual). Other shapes run exactly as umic_gemm. workspace: at least
+ * 74 CTA pairs). Each tile's k-blocks are then cut into up to 8 ranges of at least 4
+ * k-blocks, one work unit per CTA pair (per CTA for m <= 128). A unit owns whole 32-column
+ * chunks of its tile: it writes its fp32 partials of the chunks the other units own to the
+ * workspace, waits until they have written theirs, sums its own chunks over all partials
+ * in range order (deterministic) and runs the epilogue (bias, GELU, residual) on them.
+ * The units wait for one another, so a launch assumes all of them resident at once (there
+ * are never more units than CTA pairs or CTAs); a kernel on another stream that holds SMs
+ * meanwhile can keep a unit out past the wait limit, and the call then ends with
+ * UMIC_DEVERR_WAIT_TIMEOUT set instead of hanging. Other shapes run exactly as
+ * umic_gemm. workspace: at least
  * umic_gemm_workspace_bytes(m, n, k) bytes (0 when no split applies), 256-byte aligned,
  * zero-filled before its first use; every call leaves its counters at zero, except a call
  * that set UMIC_DEVERR_WAIT_TIMEOUT: zero the workspace again after one. Calls sharing

@@ -35,6 +35,19 @@
 // wave of CTAs shares both its activation rows and its weight columns in L2
 // (the reference's GROUP swizzle, linear.py:43-55).
 //
+// Split-K (umic_gemm_ws, linear only): when the output tiles would keep at most
+// half of the CTA pairs busy, each tile's k-blocks are cut into up to kMaxSplits
+// ranges, one work unit per CTA (pair), so every unit is resident at once. A unit
+// owns whole 32-column chunks of its tile; it posts its fp32 partials of the
+// other units' chunks to the workspace, counts itself in, waits (bounded) for
+// the others, bulk-copies their partials of its own chunks into its idle stage
+// ring and sums them in range order, so the result does not depend on timing.
+//
+// Launch order: the kernel is launched with programmatic stream serialization.
+// It sets up its barriers and TMEM, lets the stream's next kernel begin its own
+// set-up, then waits for the previous kernel (griddepcontrol.wait) before its
+// first load.
+//
 // Every mbarrier wait is bounded (about 5 s of SM clock); a wait that runs
 // out sets UMIC_DEVERR_WAIT_TIMEOUT, the CTA drains its outstanding work,
 // frees its TMEM and exits instead of hanging.
