@@ -144,3 +144,28 @@ def test_gemm_split_plan_on_host():
     assert L.umic_gemm_workspace_bytes(24800, 4096, 4096) == 0
     assert L.umic_gemm_workspace_bytes(3100, 4096, 4096) == 0
     assert L.umic_gemm_workspace_bytes(256, 2048, 256) == 0  # too few k-blocks to split
+
+
+def _split_plan_bytes(m, n, k, sms=148):
+    """The split-K planner's rule, restated: 256-row pair tiles (128-row single-CTA tiles
+    for m <= 128) by 256 columns; split only when the tiles fill at most half the units
+    (CTA pairs, or CTAs) and there are at least 8 k-blocks of 64; ranges = min(units per
+    tile, k-blocks / 4, 8); workspace = 4 KB of counters + 2 halves x ranges x 128 x 256
+    fp32 per tile."""
+    pair = m > 128
+    tiles = -(-m // (256 if pair else 128)) * -(-n // 256)
+    kblocks = -(-k // 64)
+    units = sms // 2 if pair else sms
+    if tiles * 2 > units or kblocks < 8:
+        return 0
+    s = min(units // tiles, kblocks // 4, 8)
+    return 0 if s < 2 else 4096 + tiles * 2 * s * 128 * 256 * 4
+
+
+def test_gemm_split_plan_matches_its_rule():
+    L = _lib.lib()
+    for m in (1, 64, 128, 129, 256, 512, 1000, 2048):
+        for n in (256, 1024, 2048, 4096, 6144):
+            for k in (256, 512, 1024, 2048, 8192):
+                assert L.umic_gemm_workspace_bytes(m, n, k) == _split_plan_bytes(m, n, k), \
+                    (m, n, k)
