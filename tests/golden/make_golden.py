@@ -13,6 +13,8 @@ What is recorded (small seeded cases, CPU):
     layouts), _gate_silu_mul_kernel and _linear_kernel (plain / bias / GELU).
     The interpreter's bf16 tl.dot is unreliable, so the two GEMM kernels are fed
     the same bf16 values carried in fp32 and their fp32 outputs are stored;
+    the same kernels again on edge shapes (4096 / 2048 / 1000 / 80 wide rows, one
+    row, inputs of large magnitude, 64-wide rotary heads, a partial last k-block);
   * the reference's eager CPU path: gate_silu_mul_eager in bf16;
   * the HF transformers eager functions the reference patches
     (apply_rotary_pos_emb, apply_rotary_pos_emb_vision, Qwen3VLTextRMSNorm);
@@ -94,6 +96,60 @@ def kernels(fixtures: dict) -> None:
     fixtures["linear"] = dict(
         x=x, w=w, b=b,
         y_fp32=linear.linear_triton(x.float(), w.float()),
+        y_bias_fp32=linear.linear_triton(x.float(), w.float(), b.float()),
+        y_gelu_fp32=linear.linear_triton(x.float(), w.float(), b.float(), act="gelu"))
+
+
+def edge_cases(fixtures: dict) -> None:
+    """More shapes through the same reference kernels, on their own seed (the cases above
+    stay as they were): the cfg4 and cfg5 row widths, a width that is not a power of two
+    (masked tail of the kernel's block), one-row inputs, a larger eps, inputs of large
+    magnitude, a 64-wide rotary head, and GEMMs whose K ends in a partial block."""
+    import torch
+    from umic.kernels import fused_ffn, layernorm, linear, rmsnorm, rope
+
+    bf = torch.bfloat16
+    g = _gen(400)
+    for tag, (rows, n, eps, scale) in {"w4096": (2, 4096, 1e-6, 1.0),
+                                       "w2048": (3, 2048, 1e-6, 1.0),
+                                       "w1000": (3, 1000, 1e-6, 1.0),
+                                       "row1": (1, 128, 1e-5, 1.0),
+                                       "big": (2, 256, 1e-6, 300.0)}.items():
+        x = (scale * torch.randn(rows, n, generator=g)).to(bf)
+        r = (scale * torch.randn(rows, n, generator=g)).to(bf)
+        w = (1 + 0.05 * torch.randn(n, generator=g)).to(bf)
+        y = rmsnorm.rmsnorm_triton(x, w, eps)
+        yn, ys = rmsnorm.add_rmsnorm_triton(x, r, w, eps)
+        fixtures[f"rmsnorm_{tag}"] = dict(x=x, r=r, w=w, eps=eps, y=y, normed=yn, summed=ys)
+    for tag, (rows, n, eps) in {"w1000": (2, 1000, 1e-6), "w80": (3, 80, 1e-5),
+                                "row1": (1, 1280, 1e-6)}.items():
+        x = torch.randn(rows, n, generator=g).to(bf)
+        r = torch.randn(rows, n, generator=g).to(bf)
+        w = torch.randn(n, generator=g).to(bf)
+        b = torch.randn(n, generator=g).to(bf)
+        y = layernorm.layernorm_triton(x, w, b, eps)
+        yn, ys = layernorm.add_layernorm_triton(x, r, w, b, eps)
+        fixtures[f"layernorm_{tag}"] = dict(x=x, r=r, w=w, b=b, eps=eps, y=y, normed=yn,
+                                            summed=ys)
+    # text layout, 64-wide heads, 2 heads x 5 positions, theta 1e4
+    qt = torch.randn(2, 5, 64, generator=g).to(bf)
+    pos = torch.arange(5).float() + 17
+    inv = 1.0 / (1e4 ** (torch.arange(0, 64, 2).float() / 64))
+    fr = pos[:, None] * inv[None]
+    emb = torch.cat((fr, fr), -1)
+    ct, st = emb.cos().to(bf), emb.sin().to(bf)
+    fixtures["rope_text_d64"] = dict(q=qt, cos=ct, sin=st, q_out=rope._apply_one(qt, ct, st, 1, 0))
+    # GEMMs with K = 72 (a partial last k-block) and M, N not multiples of the blocks
+    x = torch.randn(33, 72, generator=g).to(bf)
+    wg = (0.1 * torch.randn(72, 40, generator=g)).to(bf)
+    wu = (0.1 * torch.randn(72, 40, generator=g)).to(bf)
+    h32 = fused_ffn.gate_silu_mul_triton(x.float(), wg.float(), wu.float(), block_m=32,
+                                         block_n=32, block_k=32)
+    fixtures["gate_silu_mul_ktail"] = dict(x=x, w_gate=wg, w_up=wu, h_fp32=h32)
+    w = (0.1 * torch.randn(40, 72, generator=g)).to(bf)
+    b = torch.randn(40, generator=g).to(bf)
+    fixtures["linear_ktail"] = dict(
+        x=x, w=w, b=b,
         y_bias_fp32=linear.linear_triton(x.float(), w.float(), b.float()),
         y_gelu_fp32=linear.linear_triton(x.float(), w.float(), b.float(), act="gelu"))
 
@@ -212,6 +268,7 @@ def main() -> None:
 
     fixtures: dict = {}
     kernels(fixtures)
+    edge_cases(fixtures)
     hf_eager(fixtures)
     kv_cache_sequence(fixtures)
     torch.save(fixtures, OUT / "reference_vectors.pt")

@@ -35,7 +35,7 @@ def _same_as_rn(oracle_fp32, ref_bf16):
     assert torch.equal(oracle_fp32.to(torch.bfloat16), ref_bf16)
 
 
-@pytest.mark.parametrize("tag", ["a", "b", "c"])
+@pytest.mark.parametrize("tag", ["a", "b", "c", "w4096", "w2048", "w1000", "row1", "big"])
 def test_rmsnorm_vs_reference_kernel(gv, tag):
     c = gv[f"rmsnorm_{tag}"]
     _same_as_interpreted_kernel(oracle.rmsnorm(c["x"], c["w"], c["eps"]), c["y"])
@@ -44,7 +44,7 @@ def test_rmsnorm_vs_reference_kernel(gv, tag):
     _same_as_interpreted_kernel(summed, c["summed"])
 
 
-@pytest.mark.parametrize("tag", ["a", "b"])
+@pytest.mark.parametrize("tag", ["a", "b", "w1000", "w80", "row1"])
 def test_layernorm_vs_reference_kernel(gv, tag):
     c = gv[f"layernorm_{tag}"]
     _same_as_interpreted_kernel(oracle.layernorm(c["x"], c["w"], c["b"], c["eps"]), c["y"])
@@ -59,9 +59,10 @@ def test_rope_vs_reference_kernel(gv):
         oracle.rope_rotate_half(c["q"], c["cos"][:, None], c["sin"][:, None]), c["q_out"])
     _same_as_interpreted_kernel(
         oracle.rope_rotate_half(c["k"], c["cos"][:, None], c["sin"][:, None]), c["k_out"])
-    t = gv["rope_text"]  # [H, S, D] with [S, D] tables
-    _same_as_interpreted_kernel(oracle.rope_rotate_half(t["q"], t["cos"][None], t["sin"][None]),
-                                t["q_out"])
+    for key in ("rope_text", "rope_text_d64"):  # [H, S, D] with [S, D] tables
+        t = gv[key]
+        _same_as_interpreted_kernel(
+            oracle.rope_rotate_half(t["q"], t["cos"][None], t["sin"][None]), t["q_out"])
 
 
 def test_gemm_formulas_vs_reference_kernels(gv):
@@ -72,6 +73,18 @@ def test_gemm_formulas_vs_reference_kernels(gv):
     assert oracle.max_rel_err(c["h_eager_bf16"], h) < 1e-2
     lin = gv["linear"]
     assert oracle.max_rel_err(oracle.linear(lin["x"], lin["w"]), lin["y_fp32"]) < 1e-5
+    assert oracle.max_rel_err(oracle.linear(lin["x"], lin["w"], lin["b"]),
+                              lin["y_bias_fp32"]) < 1e-5
+    assert oracle.max_rel_err(oracle.linear(lin["x"], lin["w"], lin["b"], act="gelu"),
+                              lin["y_gelu_fp32"]) < 1e-5
+
+
+def test_gemm_formulas_with_a_partial_k_block(gv):
+    """K = 72: the reference kernels' last k-block is masked; M and N end mid-block."""
+    c = gv["gate_silu_mul_ktail"]
+    assert oracle.max_rel_err(oracle.gate_silu_mul(c["x"], c["w_gate"], c["w_up"]),
+                              c["h_fp32"]) < 1e-5
+    lin = gv["linear_ktail"]
     assert oracle.max_rel_err(oracle.linear(lin["x"], lin["w"], lin["b"]),
                               lin["y_bias_fp32"]) < 1e-5
     assert oracle.max_rel_err(oracle.linear(lin["x"], lin["w"], lin["b"], act="gelu"),
