@@ -77,15 +77,16 @@ UMIC_API int umic_set_device(int device);
 UMIC_API int umic_device_errors(uint32_t* flags, int clear);
 
 /* Test hook of the bounded-wait abort path. Arms the NEXT launch of one kernel
- * family in this process (kernel = 1: the tensor-core GEMM, umic_gemm /
+ * family in this process (kernel = 1: the tensor-core GEMM, umic_gemm / umic_gemm_ws /
  * umic_gemm_gate_silu_mul; 2: the streaming GEMV engine): in that launch CTA 0 announces
  * the bytes of its first shared-memory stage but never loads them, and every bounded wait
  * of the launch gives up after wait_limit_cycles SM cycles instead of about 5 s. The
  * stalled CTA (and its pair partner) then sets UMIC_DEVERR_WAIT_TIMEOUT, lets its copies
  * in flight land, frees its tensor memory and exits; that launch's output is undefined,
- * and the GEMV workspace counters of that launch may be left non-zero (zero the workspace
- * before its next use). Calls made after it run normally. The arm is consumed by the first
- * matching launch. kernel = 3 is not a stall: the next streaming-GEMV launch merges every
+ * and the counters in the workspace of that launch (streaming GEMV, split-K GEMM) may be
+ * left non-zero (zero the workspace before its next use). Calls made after it run
+ * normally. The arm is consumed by the first matching launch. kernel = 3 is not a
+ * stall: the next streaming-GEMV launch merges every
  * row block split between two CTAs through the general path (count, then sum), never the
  * shortcut that takes an already posted partner partial, so tests can compare the two
  * merges bit for bit (wait_limit_cycles must be positive and is otherwise ignored).
