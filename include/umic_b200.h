@@ -86,10 +86,10 @@ UMIC_API int umic_device_errors(uint32_t* flags, int clear);
  * and the counters in the workspace of that launch (streaming GEMV, split-K GEMM) may be
  * left non-zero (zero the workspace before its next use). Calls made after it run
  * normally. The arm is consumed by the first matching launch. kernel = 3 is not a
- * stall: the next streaming-GEMV launch merges every
- * row block split between two CTAs through the general path (count, then sum), never the
- * shortcut that takes an already posted partner partial, so tests can compare the two
- * merges bit for bit (wait_limit_cycles must be positive and is otherwise ignored).
+ * stall: the next streaming-GEMV launch merges every row block split between two CTAs
+ * through the general path (count, then sum), never the shortcut that takes an already
+ * posted partner partial, so tests can compare the two merges bit for bit
+ * (wait_limit_cycles must be positive and is otherwise ignored).
  * No reference counterpart: the reference has no device-side waits. */
 UMIC_API int umic_debug_stall(int kernel, int64_t wait_limit_cycles);
 
